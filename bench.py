@@ -1,0 +1,374 @@
+"""Benchmark of the STAR-KV paged low-rank decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode step of one compressed layer over the whole batch: write
+the step's new K/V codes into the paged cache, then paged low-rank decode
+attention (bf16 codes: configuration 2 of BASELINE.json, 64 sequences x 8192
+tokens). The 3.2-bit configuration 3 (64 x 16384) is measured the same way and
+reported under "q32". Inputs are seeded synthetic tensors with the configs'
+shapes and distributions (starkv_b200.workload); every step reads a >2 GB cache,
+far larger than the 126 MB L2, so no flush is needed between steps.
+
+N > 1 (torchrun): heads are sharded tensor-parallel across ranks, balanced by K
+rank (LPT), V codes replicated (the shared latent is read by every head); the
+step time is the max over ranks and `value` counts the batch's decode tokens
+once (strong scaling: the total work is fixed).
+
+--impl reference: the reference algorithm's CPU restatement (oracle/), timed on
+this host's cores on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "star-kv-serve_b200"))
+
+METRIC = "low-rank paged decode attn µs/layer & HBM GB/s; decode tok/s at 1/2/4/8 B200"
+UNIT = "decode tok/s per layer-step"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}", "--format=csv,noheader",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                mx = float(parts[2].split()[0])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def shard_layer_spec(ranks, world, rank):
+    from starkv_b200.sharding import lpt_shard
+    return lpt_shard(ranks, world)[rank]
+
+
+def build_layer(quant: bool, world: int, rank: int, device):
+    from starkv_b200.workload import make_layer, sample_ranks
+    n, L = (64, 16384) if quant else (64, 8192)
+    ranks, rv = sample_ranks(32, 0)
+    heads = list(range(32)) if world == 1 else shard_layer_spec(ranks, world, rank)
+    local = [ranks[h] for h in heads]
+    layer = make_layer([L] * n, num_heads=len(local), quant=quant, seed=0, device=device, ranks=local, v_rank=rv)
+    return layer, heads
+
+
+def run_step_fns(layer, device):
+    import torch
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode, write_kv_bf16
+    from starkv_b200 import workspace
+    g = torch.Generator(device=device).manual_seed(123)
+    n = layer.n
+    k_new = torch.randn(n, layer.k_width, generator=g, device=device).to(torch.bfloat16)
+    v_new = torch.randn(n, layer.v_rank, generator=g, device=device).to(torch.bfloat16)
+    for r, o in zip(layer.ranks, layer.offsets):
+        w = -(-r // 16) * 16
+        k_new[:, o + r:o + w] = 0
+    # the new token of sequence b sits at position L_b - 1
+    pos = torch.tensor([L - 1 for L in layer.seq_lens_host], device=device)
+    slots = (layer.block_table[torch.arange(n, device=device), pos // 16].long() * 16 + pos % 16)
+    H = layer.num_heads
+    ws = workspace.reserve(device, n, H, len(layer.ranks), layer.k_width, layer.v_rank, layer.max_seq_len)
+    out = torch.empty(n, H, 128, dtype=torch.bfloat16, device=device)
+
+    def step(q=None, kn=None, vn=None, bt=None, sl=None):
+        q = layer.query if q is None else q
+        kn = k_new if kn is None else kn
+        vn = v_new if vn is None else vn
+        bt = layer.block_table if bt is None else bt
+        sl = layer.seq_lens if sl is None else sl
+        if layer.quant:
+            pq.pack_kv(kn, vn, layer.kv_cache, slots, layer.row, layer.k_ranks, layer.k_head_offsets, layer.k_nouts)
+            return pq.paged_quant_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.row, layer.k_up,
+                                         layer.head_of_lane, layer.k_tiles, layer.v_up_by_q, layer.cos_sin_cache,
+                                         layer.scale, out=out, ws=ws)
+        write_kv_bf16(kn, vn, layer.kv_cache, slots)
+        return paged_starkv_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.k_up, layer.k_ranks,
+                                   layer.k_head_offsets, layer.k_width, layer.v_up_by_q, layer.cos_sin_cache,
+                                   layer.scale, out=out, ws=ws)
+    return step, (k_new, v_new)
+
+
+def measure(layer, device, steps, warmup, dist_on):
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+    from starkv_b200 import _lib
+    step, (k_new, v_new) = run_step_fns(layer, device)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def timed(fn, k):
+        if dist_on:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(k):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / k
+        if dist_on:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    clk = Clocks(device.index or 0)
+    ms = timed(step, steps)
+    clocks = clk.stop()
+
+    # per-kernel durations, live CUDA events on the launching stream (separate pass)
+    lib = _lib.lib()
+    lib.starkv_profile_begin(steps)
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    kms = (C.c_float * 4)()
+    ncalls = C.c_int32(0)
+    _lib.check(lib.starkv_profile_end(kms, C.byref(ncalls)), "profile")
+    per_kernel = [kms[i] / max(ncalls.value, 1) for i in range(4)]
+
+    # end to end through the public API with host buffers (pinned), H2D inputs + D2H output
+    n, H = layer.n, layer.num_heads
+    hq = layer.query.cpu().pin_memory()
+    hk, hv = k_new.cpu().pin_memory(), v_new.cpu().pin_memory()
+    hbt = layer.block_table.cpu().pin_memory()
+    hsl = layer.seq_lens.cpu().pin_memory()
+    dq, dk, dv = torch.empty_like(layer.query), torch.empty_like(k_new), torch.empty_like(v_new)
+    dbt, dsl = torch.empty_like(layer.block_table), torch.empty_like(layer.seq_lens)
+    hout = torch.empty(n, H, 128, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dbt.copy_(hbt, non_blocking=True)
+        dsl.copy_(hsl, non_blocking=True)
+        o = step(dq, dk, dv, dbt, dsl)
+        hout.copy_(o, non_blocking=True)
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = timed(e2e_step, steps)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hbt, hsl))
+    d2h = hout.numel() * hout.element_size()
+    return ms, per_kernel, clocks, e2e_ms, h2d, d2h
+
+
+def roofline_for(layer, per_kernel, hbm_peak):
+    """Dominant kernel's algorithmic bytes per launch / its event-timed duration."""
+    T = layer.kv_tokens()
+    names = ["fold", "scores", "pv", "lift"]
+    k = max(range(4), key=lambda i: per_kernel[i])
+    if layer.quant:
+        per_tok = {1: layer.k_width // 2 + 4 * len(layer.ranks), 2: 4 + layer.row.v_bytes}
+    else:
+        per_tok = {1: 2 * layer.k_width, 2: 2 * layer.v_rank}
+    alg = T * per_tok.get(k, 0)
+    ms = per_kernel[k]
+    achieved = alg / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
+    return {"kernel": names[k], "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+            "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": None,
+            "alg_bytes_per_launch": alg, "ms_per_launch": round(ms, 4),
+            "kernel_ms": {nm: round(v, 4) for nm, v in zip(names, per_kernel)}}
+
+
+def cpu_sample_time(quant: bool, seconds: float = 12.0):
+    """Reference algorithm (oracle port, numpy, all host cores) on whole sequences of
+    the same workload; returns (sequences per second, sample description)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import starkv_oracle as O
+    from starkv_b200.workload import sample_ranks
+    rng = np.random.default_rng(0)
+    ranks, rv = sample_ranks(32, 0)
+    widths, offsets, W = O.k_layout(ranks)
+    L = 16384 if quant else 8192
+    H = 32
+    q = rng.standard_normal((H, 128), dtype=np.float32)
+    k_up = np.zeros((W, 128), np.float32)
+    for r, o in zip(ranks, offsets):
+        k_up[o:o + r] = rng.standard_normal((r, 128), dtype=np.float32) / np.sqrt(r)
+    v_up = rng.standard_normal((H, rv, 128), dtype=np.float32) / np.sqrt(rv)
+    cs = O.rope_cos_sin(L)
+    row = O.QuantRow(W, H, rv)
+    if quant:
+        rows = O.pack_rows(rng.standard_normal((L, W), dtype=np.float32),
+                           rng.standard_normal((L, rv), dtype=np.float32), row, ranks)
+    else:
+        kc = rng.standard_normal((L, W), dtype=np.float32)
+        vc = rng.standard_normal((L, rv), dtype=np.float32)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        if quant:
+            kd, vd = O.unpack_rows(rows, row, ranks)
+            O.attend_one(q, kd, vd, k_up, ranks, offsets, 1, v_up, cs, 128 ** -0.5, dtype=np.float32)
+        else:
+            O.attend_one(q, kc, vc, k_up, ranks, offsets, 1, v_up, cs, 128 ** -0.5, dtype=np.float32)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 64:
+            break
+    return done / el, f"{done} sequence(s) x {L} tokens, 32 heads, float32 numpy (oracle port)"
+
+
+def ours(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if dist_on:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
+    hbm_peak, tf_peak, peak_kind = peaks()
+    res = {}
+    for quant in (False, True):
+        layer, heads = build_layer(quant, world, rank, device)
+        ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on)
+        res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
+                          d2h=d2h, alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
+                          roof=roofline_for(layer, per_kernel, hbm_peak))
+        del layer
+        torch.cuda.empty_cache()
+    if rank == 0:
+        b = res[False]
+        n = b["layer"].n if False else 64
+        cpu_rate, cpu_desc = (None, None)
+        if world == 1:
+            cpu_rate, cpu_desc = cpu_sample_time(False)
+        q = res[True]
+        line = {
+            "metric": METRIC, "value": round(n / (b["ms"] * 1e-3), 1), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(b["ms"], 4), "us_per_layer": round(b["ms"] * 1e3, 1),
+            "hbm_gbs": round(b["alg"] / (b["ms"] * 1e-3) / 1e9, 1),
+            "hbm_frac_step": round(b["alg"] / (b["ms"] * 1e-3) / 1e9 / hbm_peak, 4),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
+                                   "32 heads x 128, page 16, cache write + decode per step",
+                       "batch": 64, "context": 8192, "heads_per_gpu": 32 // world,
+                       "parallelism": f"tp{world} (heads)" if world > 1 else "single",
+                       "l2": "inputs (2.9 GB cache) larger than L2; no flush"},
+            "roofline": dict(b["roof"], peak_kind=peak_kind),
+            "e2e": {"value": round(n / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": b["h2d"], "d2h_bytes_per_step": b["d2h"],
+                    "ms_per_step": round(b["e2e_ms"], 4)},
+            "gpu_launches": 5 * args.steps,
+            "clocks": b["clocks"],
+            "q32": {"workload": "config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
+                    "value": round(64 / (q["ms"] * 1e-3), 1), "unit": UNIT, "ms_per_step": round(q["ms"], 4),
+                    "us_per_layer": round(q["ms"] * 1e3, 1),
+                    "hbm_gbs": round(q["alg"] / (q["ms"] * 1e-3) / 1e9, 1),
+                    "hbm_frac_step": round(q["alg"] / (q["ms"] * 1e-3) / 1e9 / hbm_peak, 4),
+                    "tflops": round(q["flops"] / (q["ms"] * 1e-3) / 1e12, 1),
+                    "roofline": dict(q["roof"], peak_kind=peak_kind),
+                    "e2e_ms_per_step": round(q["e2e_ms"], 4), "clocks": q["clocks"]},
+        }
+        if cpu_rate is not None:
+            line["cpu_baseline"] = {"value": round(cpu_rate, 3), "unit": UNIT, "cores": os.cpu_count(),
+                                    "kind": "port", "sample": cpu_desc}
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, desc = cpu_sample_time(False, seconds=2.0)
+        if i >= args.warmup:
+            rates.append(r)
+    v = statistics.median(rates)
+    line = {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "impl": "reference",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
+                                   "32 heads x 128 (CPU: reference algorithm, whole sequences per sample)"},
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    if a.impl == "reference":
+        reference(a)
+    else:
+        ours(a)
+
+
+if __name__ == "__main__":
+    main()

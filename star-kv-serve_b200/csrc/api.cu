@@ -1,0 +1,389 @@
+// C ABI entry points of the decode path (include/starkv_b200.h): argument
+// validation, workspace layout, TMA descriptor encoding, launch order.
+//
+// One decode call = 4 launches on the caller's stream, no host synchronisation,
+// no allocation:
+//   fold_kernel -> scores_kernel (tcgen05) -> pv_kernel (tcgen05) -> lift_kernel
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <mutex>
+
+#include "starkv_common.cuh"
+#include "starkv_kernels.h"
+
+namespace starkv {
+
+namespace {
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  bool sm100 = false;
+};
+
+int device_info(DeviceInfo& info) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return STARKV_ECUDA;
+  static DeviceInfo cache[64];
+  static std::once_flag flags[64];
+  if (dev < 0 || dev >= 64) return STARKV_ENODEV;
+  std::call_once(flags[dev], [dev] {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev].sms = sms;
+    cache[dev].sm100 = (major == 10 && minor == 0);
+  });
+  info = cache[dev];
+  return info.sm100 ? STARKV_OK : STARKV_ENODEV;
+}
+
+// Tiled TMA descriptor; dims[0] is the contiguous one, strides in bytes for dims 1..rank-1.
+int make_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return STARKV_ECUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return STARKV_EALIGN;
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides_bytes[i] & 15) return STARKV_EALIGN;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), reinterpret_cast<const cuuint64_t*>(dims),
+                  reinterpret_cast<const cuuint64_t*>(strides_bytes), reinterpret_cast<const cuuint32_t*>(box), estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? STARKV_OK : STARKV_EALIGN;
+}
+
+// Optional per-kernel timing (bench only): a pool of CUDA events recorded on the
+// launch stream around each of the 4 decode kernels.
+struct Profile {
+  bool on = false;
+  int max_calls = 0, calls = 0;
+  cudaEvent_t* ev = nullptr;   // [max_calls][5]
+};
+Profile g_prof;
+
+bool is_float_dtype(int d) { return d == STARKV_BF16 || d == STARKV_F16 || d == STARKV_F32; }
+
+}  // namespace
+
+Workspace workspace_layout(int n, int num_heads, int num_kv_heads, int k_width, int v_rank, int max_seq_len) {
+  Workspace w{};
+  const int group = num_kv_heads > 0 ? num_heads / num_kv_heads : 1;
+  w.n_tiles = (max_seq_len + 127) / 128;
+  if (w.n_tiles < 1) w.n_tiles = 1;
+  w.l_pad = w.n_tiles * 128;
+  size_t off = 0;
+  w.status = off; off += 256;
+  w.ab = off; off = align256(off + (size_t)n * group * k_width * 128 * 2);
+  w.cs = off; off = align256(off + (size_t)w.l_pad * 128 * 2);
+  w.e16 = off; off = align256(off + (size_t)n * num_heads * w.l_pad * 2);
+  w.m_tile = off; off = align256(off + (size_t)n * num_heads * w.n_tiles * 4);
+  w.l_tile = off; off = align256(off + (size_t)n * num_heads * w.n_tiles * 4);
+  w.m_seq = off; off = align256(off + (size_t)n * num_heads * 4);
+  w.pv = off; off = align256(off + (size_t)n * num_heads * v_rank * 4);
+  w.total = off;
+  return w;
+}
+
+static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_bytes, cudaStream_t stream, bool quant) {
+  if (!a) return STARKV_EINVAL;
+  DeviceInfo dev;
+  int st = device_info(dev);
+  if (st) return st;
+  // ---- shape / type validation (reference asserts: paged_decode.py:172-174, paged_quant.py:374-376) ----
+  if (a->n < 0 || a->num_heads <= 0 || a->num_kv_heads <= 0 || a->num_heads % a->num_kv_heads) return STARKV_EINVAL;
+  if (a->n == 0) return STARKV_OK;
+  if (a->head_dim != 128) return STARKV_EINVAL;
+  if (a->k_width <= 0 || a->k_width % 16 || a->v_rank <= 0) return STARKV_EINVAL;
+  if (a->max_seq_len <= 0 || a->cs_rows < a->max_seq_len) return STARKV_EINVAL;
+  if (a->block_size <= 0 || a->block_size % 16 || a->num_blocks <= 0) return STARKV_EINVAL;
+  if (a->num_heads > 128 || a->max_blocks <= 0) return STARKV_EINVAL;
+  if (!a->query || !a->kv_cache || !a->block_table || !a->seq_lens || !a->k_up || !a->v_up_by_q ||
+      !a->cos_sin_cache || !a->out)
+    return STARKV_EINVAL;
+  if (!is_float_dtype(a->q_dtype) || !is_float_dtype(a->k_up_dtype) || !is_float_dtype(a->v_up_dtype) ||
+      !is_float_dtype(a->cs_dtype) || !is_float_dtype(a->out_dtype))
+    return STARKV_EDTYPE;
+  if (a->cache_stride[2] != 1) return STARKV_EALIGN;
+  const int group = a->num_heads / a->num_kv_heads;
+  if (quant) {
+    if (a->cache_dtype != STARKV_U8) return STARKV_EDTYPE;
+    if (group != 1) return STARKV_EINVAL;   // 4-bit decode: MHA (paged_quant.py:374)
+    if (!a->head_of_lane || !a->tile_head || !a->tile_nout || !a->tile_last) return STARKV_EINVAL;
+    if (a->ks_off != a->k_width / 2 || a->vs_off != a->ks_off + 4 * a->num_kv_heads || a->vq_off != a->vs_off + 4)
+      return STARKV_EINVAL;
+    if (a->v_nout < 0 || a->v_nout > a->v_rank || a->v_nbo != (a->v_nout + 1) / 2 ||
+        a->v_bytes != a->v_nbo + (a->v_rank - a->v_nout + 1) / 2 || a->row_nbytes < a->vq_off + a->v_bytes)
+      return STARKV_EINVAL;
+  } else {
+    if (a->cache_dtype != STARKV_BF16 && a->cache_dtype != STARKV_F16) return STARKV_EDTYPE;
+    if (!a->k_ranks || !a->k_head_offsets) return STARKV_EINVAL;
+  }
+
+  const Workspace ws = workspace_layout(a->n, a->num_heads, a->num_kv_heads, a->k_width, a->v_rank, a->max_seq_len);
+  if (!workspace || ws_bytes < ws.total) return STARKV_EWORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return STARKV_EALIGN;
+  uint8_t* W = reinterpret_cast<uint8_t*>(workspace);
+  int32_t* status = reinterpret_cast<int32_t*>(W + ws.status);
+  __half* ab = reinterpret_cast<__half*>(W + ws.ab);
+  __half* cs16 = reinterpret_cast<__half*>(W + ws.cs);
+  __half* e16 = reinterpret_cast<__half*>(W + ws.e16);
+  float* m_tile = reinterpret_cast<float*>(W + ws.m_tile);
+  float* l_tile = reinterpret_cast<float*>(W + ws.l_tile);
+  float* m_seq = reinterpret_cast<float*>(W + ws.m_seq);
+  float* pv = reinterpret_cast<float*>(W + ws.pv);
+
+  // ---- TMA descriptors ----
+  CUtensorMap tm_cs, tm_ab, tm_codes, tm_wide;
+  {
+    const uint64_t dims[2] = {128, (uint64_t)ws.l_pad};
+    const uint64_t str[1] = {256};
+    const uint32_t box[2] = {64, 128};
+    if ((st = make_map(&tm_cs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cs16, dims, str, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  }
+  {
+    const uint64_t dims[2] = {128, (uint64_t)a->n * group * a->k_width};
+    const uint64_t str[1] = {256};
+    const uint32_t box[2] = {64, 128};
+    if ((st = make_map(&tm_ab, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ab, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  }
+  const int es = quant ? 1 : 2;
+  const uint64_t row_elems = quant ? (uint64_t)a->row_nbytes : (uint64_t)(a->k_width + a->v_rank);
+  if (a->cache_stride[1] < (int64_t)row_elems || a->cache_stride[0] < a->cache_stride[1] * a->block_size)
+    return STARKV_EINVAL;
+  {
+    const uint64_t dims[3] = {row_elems, (uint64_t)a->block_size, (uint64_t)a->num_blocks};
+    const uint64_t str[2] = {(uint64_t)a->cache_stride[1] * es, (uint64_t)a->cache_stride[0] * es};
+    const CUtensorMapDataType dt = quant ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const uint32_t box[3] = {64, 16, 1};   // bf16: 64 lanes = 128 B; 3.2-bit: 64 B = 128 lanes
+    if ((st = make_map(&tm_codes, dt, 3, a->kv_cache, dims, str, box,
+                       quant ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    if (quant) {
+      const uint32_t box2[3] = {128, 16, 1};   // scale / V byte boxes
+      if ((st = make_map(&tm_wide, dt, 3, a->kv_cache, dims, str, box2, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    } else {
+      tm_wide = tm_codes;
+    }
+  }
+
+  // ---- fold + table + init ----
+  FoldParams fp{};
+  fp.q = a->query; fp.q_s0 = a->q_stride[0]; fp.q_s1 = a->q_stride[1]; fp.q_s2 = a->q_stride[2];
+  fp.q_dtype = a->q_dtype;
+  fp.k_up = a->k_up; fp.ku_s0 = a->k_up_stride[0]; fp.ku_s1 = a->k_up_stride[1]; fp.k_up_dtype = a->k_up_dtype;
+  fp.head_of_lane = quant ? a->head_of_lane : nullptr;
+  fp.k_ranks = a->k_ranks; fp.k_head_offsets = a->k_head_offsets;
+  fp.n = a->n; fp.num_heads = a->num_heads; fp.num_kv_heads = a->num_kv_heads; fp.group = group;
+  fp.k_width = a->k_width; fp.head_dim = a->head_dim; fp.scale = a->scale; fp.ab = ab;
+  fp.cs = a->cos_sin_cache; fp.cs_s0 = a->cs_stride[0]; fp.cs_s1 = a->cs_stride[1]; fp.cs_dtype = a->cs_dtype;
+  fp.cs_rows = a->cs_rows; fp.cs16 = cs16; fp.l_pad = ws.l_pad; fp.max_seq_len = a->max_seq_len;
+  fp.m_seq = m_seq; fp.m_count = a->n * a->num_heads;
+  fp.pv = pv; fp.pv_count = (int64_t)a->n * a->num_heads * a->v_rank;
+  fp.status = status;
+  cudaEvent_t* pev = nullptr;
+  if (g_prof.on && g_prof.calls < g_prof.max_calls) pev = g_prof.ev + 5 * g_prof.calls++;
+  if (pev) cudaEventRecord(pev[0], stream);
+  if ((st = launch_fold(fp, quant, stream))) return st;
+  if (pev) cudaEventRecord(pev[1], stream);
+
+  // ---- scores ----
+  ScoresParams sp{};
+  sp.seq_lens = a->seq_lens; sp.block_table = a->block_table; sp.bt_s0 = a->bt_stride[0]; sp.bt_s1 = a->bt_stride[1];
+  sp.max_blocks = a->max_blocks;
+  sp.n = a->n; sp.num_heads = a->num_heads; sp.num_kv_heads = a->num_kv_heads; sp.group = group;
+  sp.k_width = a->k_width; sp.num_blocks = a->num_blocks; sp.block_size = a->block_size;
+  sp.max_seq_len = a->max_seq_len; sp.cache_dtype = a->cache_dtype;
+  sp.k_ranks = a->k_ranks; sp.k_head_offsets = a->k_head_offsets;
+  sp.tile_head = a->tile_head; sp.tile_nout = a->tile_nout; sp.tile_last = a->tile_last;
+  if (quant) {
+    sp.ks_off = a->ks_off;
+    sp.ks_x0 = a->ks_off & ~15;
+    sp.ks_boxes = (a->ks_off + 4 * a->num_kv_heads - sp.ks_x0 + 127) / 128;
+    if (sp.ks_boxes > 3) return STARKV_EINVAL;
+  }
+  sp.e16 = e16; sp.m_tile = m_tile; sp.l_tile = l_tile; sp.m_seq = m_seq;
+  sp.l_pad = ws.l_pad; sp.n_tiles = ws.n_tiles; sp.status = status;
+  if ((st = launch_scores(quant, tm_cs, tm_ab, tm_codes, tm_wide, sp, dev.sms, stream))) return st;
+  if (pev) cudaEventRecord(pev[2], stream);
+
+  // ---- P.V ----
+  PvParams pp{};
+  pp.seq_lens = a->seq_lens; pp.block_table = a->block_table; pp.bt_s0 = a->bt_stride[0]; pp.bt_s1 = a->bt_stride[1];
+  pp.max_blocks = a->max_blocks;
+  pp.n = a->n; pp.num_heads = a->num_heads; pp.k_width = a->k_width; pp.v_rank = a->v_rank;
+  pp.num_blocks = a->num_blocks; pp.block_size = a->block_size; pp.max_seq_len = a->max_seq_len;
+  pp.nh = ((a->num_heads + 15) / 16) * 16;
+  pp.cache_dtype = a->cache_dtype;
+  if (quant) {
+    pp.v_nout = a->v_nout; pp.v_nbo = a->v_nbo; pp.v_bytes = a->v_bytes; pp.vq_off = a->vq_off;
+    pp.vs_off = a->vs_off;
+    pp.vx0 = a->vs_off & ~15;
+    pp.v_boxes = (a->vq_off + a->v_bytes - pp.vx0 + 127) / 128;
+    pp.t_out = (a->v_nout + 127) / 128;
+    pp.n_mtiles = pp.t_out + (a->v_rank - a->v_nout + 127) / 128;
+  } else {
+    pp.n_mtiles = (a->v_rank + 127) / 128;
+  }
+  int mtpr = pp.n_mtiles;
+  if (mtpr * pp.nh > 512) mtpr = 512 / pp.nh;
+  for (;;) {
+    pp.mt_per_range = mtpr;
+    if (pv_smem_bytes(quant, pp) <= 227 * 1024 && mtpr >= 1) {
+      // at least two pipeline stages
+      const int stage = (quant ? pp.v_boxes * 2048 + mtpr * 4096 : mtpr * 4096) + 2 * pp.nh * 32;
+      if (2 * ((stage + 1023) & ~1023) <= 200 * 1024) break;
+    }
+    if (--mtpr < 1) return STARKV_EINVAL;
+  }
+  pp.n_ranges = (pp.n_mtiles + mtpr - 1) / mtpr;
+  pp.mt_per_range = (pp.n_mtiles + pp.n_ranges - 1) / pp.n_ranges;   // balance the ranges
+  pp.e16 = e16; pp.m_tile = m_tile; pp.m_seq = m_seq; pp.pv = pv;
+  pp.l_pad = ws.l_pad; pp.n_tiles = ws.n_tiles; pp.status = status;
+  if ((st = launch_pv(quant, tm_wide, pp, dev.sms, stream))) return st;
+  if (pev) cudaEventRecord(pev[3], stream);
+
+  // ---- lift ----
+  LiftParams lp{};
+  lp.pv = pv; lp.m_tile = m_tile; lp.l_tile = l_tile; lp.m_seq = m_seq;
+  lp.v_up = a->v_up_by_q; lp.vu_s0 = a->v_up_stride[0]; lp.vu_s1 = a->v_up_stride[1]; lp.vu_s2 = a->v_up_stride[2];
+  lp.v_up_dtype = a->v_up_dtype;
+  lp.out = a->out; lp.o_s0 = a->out_stride[0]; lp.o_s1 = a->out_stride[1]; lp.o_s2 = a->out_stride[2];
+  lp.out_dtype = a->out_dtype;
+  lp.seq_lens = a->seq_lens; lp.n = a->n; lp.num_heads = a->num_heads; lp.v_rank = a->v_rank;
+  lp.head_dim = a->head_dim; lp.n_tiles = ws.n_tiles; lp.max_seq_len = a->max_seq_len;
+  st = launch_lift(lp, stream);
+  if (pev) cudaEventRecord(pev[4], stream);
+  return st;
+}
+
+}  // namespace starkv
+
+extern "C" {
+
+size_t starkv_decode_workspace_bytes(int32_t n, int32_t num_heads, int32_t num_kv_heads, int32_t k_width,
+                                     int32_t v_rank, int32_t max_seq_len) {
+  if (n < 0 || num_heads <= 0 || num_kv_heads <= 0 || k_width < 0 || v_rank < 0) return 0;
+  return starkv::workspace_layout(n, num_heads, num_kv_heads, k_width, v_rank, max_seq_len).total;
+}
+
+int starkv_paged_decode_bf16(const StarKVDecodeArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  return starkv::decode_impl(args, workspace, workspace_bytes, (cudaStream_t)stream, false);
+}
+
+int starkv_paged_decode_q32(const StarKVDecodeArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  return starkv::decode_impl(args, workspace, workspace_bytes, (cudaStream_t)stream, true);
+}
+
+int starkv_fold_q(const void* query, const int64_t q_stride[3], int32_t q_dtype, const void* k_up,
+                  const int64_t k_up_stride[2], int32_t k_up_dtype, const int32_t* head_of_lane, int32_t n,
+                  int32_t num_heads, int32_t k_width, float scale, void* ab_out, void* stream) {
+  using namespace starkv;
+  if (!query || !k_up || !head_of_lane || !ab_out || n < 0 || num_heads <= 0 || k_width <= 0) return STARKV_EINVAL;
+  if (n == 0) return STARKV_OK;
+  FoldParams fp{};
+  fp.q = query; fp.q_s0 = q_stride[0]; fp.q_s1 = q_stride[1]; fp.q_s2 = q_stride[2]; fp.q_dtype = q_dtype;
+  fp.k_up = k_up; fp.ku_s0 = k_up_stride[0]; fp.ku_s1 = k_up_stride[1]; fp.k_up_dtype = k_up_dtype;
+  fp.head_of_lane = head_of_lane;
+  fp.n = n; fp.num_heads = num_heads; fp.num_kv_heads = num_heads; fp.group = 1; fp.k_width = k_width;
+  fp.head_dim = 128; fp.scale = scale; fp.ab = reinterpret_cast<__half*>(ab_out);
+  fp.l_pad = 0; fp.m_count = 0; fp.pv_count = 0;
+  return launch_fold(fp, true, (cudaStream_t)stream);
+}
+
+int starkv_read_status(void* workspace, int32_t* host_status, int32_t reset, void* stream) {
+  if (!workspace || !host_status) return STARKV_EINVAL;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (cudaMemcpyAsync(host_status, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return STARKV_ECUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return STARKV_ECUDA;
+  if (reset && cudaMemsetAsync(workspace, 0, sizeof(int32_t), s) != cudaSuccess) return STARKV_ECUDA;
+  return STARKV_OK;
+}
+
+size_t starkv_status_offset(void) { return 0; }
+
+int starkv_profile_begin(int32_t max_calls) {
+  using namespace starkv;
+  if (max_calls <= 0) return STARKV_EINVAL;
+  if (g_prof.ev) {
+    for (int i = 0; i < 5 * g_prof.max_calls; ++i) cudaEventDestroy(g_prof.ev[i]);
+    delete[] g_prof.ev;
+  }
+  g_prof.ev = new cudaEvent_t[5 * max_calls];
+  for (int i = 0; i < 5 * max_calls; ++i)
+    if (cudaEventCreate(&g_prof.ev[i]) != cudaSuccess) return STARKV_ECUDA;
+  g_prof.max_calls = max_calls;
+  g_prof.calls = 0;
+  g_prof.on = true;
+  return STARKV_OK;
+}
+
+int starkv_profile_end(float* kernel_ms, int32_t* calls) {
+  using namespace starkv;
+  if (!kernel_ms || !calls) return STARKV_EINVAL;
+  g_prof.on = false;
+  for (int k = 0; k < 4; ++k) kernel_ms[k] = 0.f;
+  for (int c = 0; c < g_prof.calls; ++c) {
+    cudaEvent_t* e = g_prof.ev + 5 * c;
+    if (cudaEventSynchronize(e[4]) != cudaSuccess) return STARKV_ECUDA;
+    for (int k = 0; k < 4; ++k) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, e[k], e[k + 1]) != cudaSuccess) return STARKV_ECUDA;
+      kernel_ms[k] += ms;
+    }
+  }
+  *calls = g_prof.calls;
+  return STARKV_OK;
+}
+
+size_t starkv_abi_sizeof(int32_t which) {
+  switch (which) {
+    case 0: return sizeof(StarKVDecodeArgs);
+    case 1: return sizeof(StarKVPackArgs);
+    case 2: return sizeof(StarKVCacheWriteArgs);
+    default: return 0;
+  }
+}
+
+const char* starkv_version(void) { return "starkv_b200 1.0 (abi 1, sm_100a)"; }
+
+const char* starkv_strerror(int status) {
+  switch (status) {
+    case STARKV_OK: return "ok";
+    case STARKV_EINVAL: return "invalid argument or unsupported shape";
+    case STARKV_EALIGN: return "pointer or stride alignment not supported";
+    case STARKV_EDTYPE: return "unsupported element type";
+    case STARKV_EWORKSPACE: return "workspace missing or too small";
+    case STARKV_ECUDA: return "CUDA call failed";
+    case STARKV_ENODEV: return "current device is not sm_100";
+    case STARKV_EBOUNDS: return "index out of range (recorded on device)";
+    case STARKV_ETIMEOUT: return "pipeline wait expired on device";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+// Internal launch interface between the C-ABI layer (api.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace starkv {
+
+// Workspace layout of one decode call (offsets in bytes, 256-aligned).
+struct Workspace {
+  size_t status;     // int32 status word (+ padding)
+  size_t ab;         // f16 [n, group, k_width, 128]   query folded into U (x scale)
+  size_t cs;         // f16 [l_pad, 128]                rotary table rows 0..l_pad-1
+  size_t e16;        // f16 [n, num_heads, l_pad]       exp(logit - tile max)
+  size_t m_tile;     // f32 [n, num_heads, n_tiles]     tile max
+  size_t l_tile;     // f32 [n, num_heads, n_tiles]     tile sum of exp
+  size_t m_seq;      // f32 [n, num_heads]              sequence max
+  size_t pv;         // f32 [n, num_heads, v_rank]      sum_t p_t * V_t (unnormalised)
+  size_t total;
+  int l_pad, n_tiles;
+};
+
+Workspace workspace_layout(int n, int num_heads, int num_kv_heads, int k_width, int v_rank, int max_seq_len);
+
+struct ScoresParams {
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int64_t bt_s0, bt_s1;
+  int max_blocks;
+  int n, num_heads, num_kv_heads, group, k_width, num_blocks, block_size, max_seq_len;
+  int cache_dtype;
+  const int32_t* k_ranks;
+  const int32_t* k_head_offsets;
+  const int32_t* tile_head;
+  const int32_t* tile_nout;
+  const int32_t* tile_last;
+  int ks_off, ks_x0, ks_boxes;     // 3.2-bit: K scales at ks_off; boxes of 128 B from ks_x0
+  __half* e16;
+  float* m_tile;
+  float* l_tile;
+  float* m_seq;
+  int l_pad, n_tiles;
+  int32_t* status;
+};
+
+struct PvParams {
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int64_t bt_s0, bt_s1;
+  int max_blocks;
+  int n, num_heads, k_width, v_rank, num_blocks, block_size, max_seq_len;
+  int nh;                 // MMA N: num_heads rounded up to a multiple of 16
+  int n_mtiles;           // 128-channel tiles over the V code (all ranges)
+  int mt_per_range;       // tiles handled per work item (TMEM columns = mt_per_range * nh)
+  int n_ranges;
+  int cache_dtype;
+  // 3.2-bit V layout (paged_quant.QuantRow)
+  int v_nout, v_nbo, v_bytes, vq_off, vs_off, vx0, v_boxes;
+  int t_out;              // tiles over the outlier block (the rest cover inliers)
+  const __half* e16;
+  const float* m_tile;
+  const float* m_seq;
+  float* pv;
+  int l_pad, n_tiles;
+  int32_t* status;
+};
+
+struct LiftParams {
+  const float* pv;        // [n, H, rv]
+  const float* m_tile;
+  const float* l_tile;
+  const float* m_seq;
+  const void* v_up; int64_t vu_s0, vu_s1, vu_s2; int v_up_dtype;   // [H, rv, Hd]
+  void* out; int64_t o_s0, o_s1, o_s2; int out_dtype;              // [n, H, Hd]
+  const int32_t* seq_lens;
+  int n, num_heads, v_rank, head_dim, n_tiles, max_seq_len;
+};
+
+struct FoldParams {
+  const void* q; int64_t q_s0, q_s1, q_s2; int q_dtype;
+  const void* k_up; int64_t ku_s0, ku_s1; int k_up_dtype;
+  const int32_t* head_of_lane;     // 3.2-bit path (reference semantics: no rank mask)
+  const int32_t* k_ranks;          // bf16 path: lanes past a head's rank get zero rows
+  const int32_t* k_head_offsets;
+  int n, num_heads, num_kv_heads, group, k_width, head_dim;
+  float scale;
+  __half* ab;                      // [n, group, W, 128]
+  // rotary table -> f16 copy
+  const void* cs; int64_t cs_s0, cs_s1; int cs_dtype; int cs_rows;
+  __half* cs16; int l_pad, max_seq_len;
+  // per-call initialisation
+  float* m_seq; int m_count;
+  float* pv; int64_t pv_count;
+  int32_t* status;
+};
+
+size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int ks_boxes);
+size_t pv_smem_bytes(bool quant, const PvParams& p);
+
+int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream);
+int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_codes,
+                  const CUtensorMap& tm_scales, const ScoresParams& p, int num_sms, cudaStream_t stream);
+int launch_pv(bool quant, const CUtensorMap& tm_v, const PvParams& p, int num_sms, cudaStream_t stream);
+int launch_lift(const LiftParams& p, cudaStream_t stream);
+
+}  // namespace starkv

@@ -1,0 +1,102 @@
+"""Paged STAR-KV decode attention over bf16 / f16 codes, on the sm_100a library.
+
+Drop-in for ``starkv_serve/kernels/paged_decode.py``: ``paged_starkv_decode`` keeps
+the reference signature and result (paged_decode.py:150-226) and is called from
+the same place (attention.py:204-207). The work runs in
+``starkv_paged_decode_bf16`` (include/starkv_b200.h): fold the query into the K
+up-projection, tcgen05 logits over the paged K codes, tcgen05 P.V over the shared
+V codes, lift with ``v_up_by_q``. No torch math runs on this path and there is no
+fallback: if the native library is missing the call raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib, workspace
+
+# Kept for call-site compatibility with the reference (paged_decode.py:22-28);
+# the tile shapes of this implementation are fixed inside the library.
+BLOCK_L = 128
+TARGET_V_PROGRAMS = 256
+
+
+def paged_starkv_decode(
+    query: torch.Tensor,          # [n, H_q, head_dim], RoPE already applied
+    kv_cache: torch.Tensor,       # [num_blocks, block_size, width] (inner stride 1)
+    block_table: torch.Tensor,    # [n, max_blocks] int32
+    seq_lens: torch.Tensor,       # [n] int32, including the token just written
+    max_seq_len: int,             # host-side bound on seq_lens (max_model_len in a CUDA graph)
+    k_up: torch.Tensor,           # [k_width, head_dim]  U^T, heads side by side
+    k_ranks: torch.Tensor,        # [H_kv] int32
+    k_head_offsets: torch.Tensor, # [H_kv] int32
+    k_width: int,
+    v_up_by_q: torch.Tensor,      # [H_q, v_rank, head_dim]
+    cos_sin_cache: torch.Tensor,  # [max_positions, head_dim] = cat(cos, sin)
+    scale: float,
+    v_programs: int = TARGET_V_PROGRAMS,  # accepted for compatibility; work split is automatic
+    *,
+    out: torch.Tensor | None = None,
+    ws: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Returns the attention output per query head, ``[n, H_q, head_dim]`` in
+    ``v_up_by_q.dtype`` (paged_decode.py:166)."""
+    n, num_heads, head_dim = query.shape
+    num_kv_heads = k_ranks.numel()
+    v_rank = v_up_by_q.shape[1]
+    # the reference's own preconditions (paged_decode.py:172-174)
+    assert head_dim % 2 == 0 and num_heads % num_kv_heads == 0
+    assert kv_cache.shape[-1] == k_width + v_rank, "cache width != K codes + V codes"
+    assert cos_sin_cache.shape[-1] == head_dim and cos_sin_cache.shape[0] >= max_seq_len
+    if out is None:
+        out = torch.empty((n, num_heads, head_dim), dtype=v_up_by_q.dtype, device=query.device)
+    if n == 0:
+        return out
+    k_ranks = k_ranks if k_ranks.dtype == torch.int32 else k_ranks.to(torch.int32)
+    k_head_offsets = k_head_offsets if k_head_offsets.dtype == torch.int32 else k_head_offsets.to(torch.int32)
+    block_table = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    seq_lens = seq_lens if seq_lens.dtype == torch.int32 else seq_lens.to(torch.int32)
+    need = workspace.bytes_needed(n, num_heads, num_kv_heads, k_width, v_rank, max_seq_len)
+    if ws is None:
+        ws = workspace.get(query.device, need)
+    a = _lib.DecodeArgs()
+    a.query, a.q_stride, a.q_dtype = query.data_ptr(), _lib.i64s(query.stride()), _lib.dtype_code(query)
+    a.kv_cache, a.cache_stride, a.cache_dtype = kv_cache.data_ptr(), _lib.i64s(kv_cache.stride()), \
+        _lib.dtype_code(kv_cache)
+    a.num_blocks, a.block_size = kv_cache.shape[0], kv_cache.shape[1]
+    a.block_table, a.bt_stride, a.max_blocks = block_table.data_ptr(), _lib.i64s(block_table.stride()), \
+        block_table.shape[1]
+    a.seq_lens = seq_lens.data_ptr()
+    a.n, a.num_heads, a.num_kv_heads, a.head_dim = n, num_heads, num_kv_heads, head_dim
+    a.max_seq_len = int(max_seq_len)
+    a.k_up, a.k_up_stride, a.k_up_dtype = k_up.data_ptr(), _lib.i64s(k_up.stride()), _lib.dtype_code(k_up)
+    a.k_ranks, a.k_head_offsets, a.k_width = k_ranks.data_ptr(), k_head_offsets.data_ptr(), int(k_width)
+    a.v_up_by_q, a.v_up_stride, a.v_up_dtype = v_up_by_q.data_ptr(), _lib.i64s(v_up_by_q.stride()), \
+        _lib.dtype_code(v_up_by_q)
+    a.v_rank = v_rank
+    a.cos_sin_cache, a.cs_stride, a.cs_dtype, a.cs_rows = cos_sin_cache.data_ptr(), \
+        _lib.i64s(cos_sin_cache.stride()), _lib.dtype_code(cos_sin_cache), cos_sin_cache.shape[0]
+    a.scale = float(scale)
+    a.out, a.out_stride, a.out_dtype = out.data_ptr(), _lib.i64s(out.stride()), _lib.dtype_code(out)
+    st = _lib.lib().starkv_paged_decode_bf16(a, ws.data_ptr(), ws.numel(), _lib.stream_ptr(query.device))
+    _lib.check(st, "paged_starkv_decode")
+    return out
+
+
+def write_kv_bf16(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                  status: torch.Tensor | None = None) -> None:
+    """``cache[slot // bs, slot % bs] = cat(key, value)`` with slot -1 sent to the
+    null block (attention.py:179-185), on the library's cache-write kernel."""
+    n = key.shape[0]
+    if n == 0:
+        return
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    a = _lib.CacheWriteArgs()
+    a.key, a.key_stride0, a.key_dtype = key.data_ptr(), key.stride(0), _lib.dtype_code(key)
+    a.value, a.value_stride0, a.value_dtype = value.data_ptr(), value.stride(0), _lib.dtype_code(value)
+    a.cache, a.cache_stride, a.cache_dtype = kv_cache.data_ptr(), _lib.i64s(kv_cache.stride()), \
+        _lib.dtype_code(kv_cache)
+    a.num_blocks, a.block_size = kv_cache.shape[0], kv_cache.shape[1]
+    a.slot_mapping, a.slot_dtype = slot_mapping.data_ptr(), _lib.dtype_code(slot_mapping)
+    a.n, a.k_width, a.v_rank = n, key.shape[1], value.shape[1]
+    a.status = None if status is None else status.data_ptr()
+    _lib.check(_lib.lib().starkv_cache_write_bf16(a, _lib.stream_ptr(kv_cache.device)), "write_kv_bf16")

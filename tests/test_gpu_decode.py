@@ -1,0 +1,224 @@
+"""GPU parity of the sm_100a decode path against the CPU oracle and the
+reference-generated golden fixtures (tests/golden/).
+
+Tolerance (the target's): attention output within 2e-2 abs + 1e-2 rel of the
+fp32/fp64 reference math; packed bytes and dequantized codes bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import starkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda", 0)
+
+
+def assert_close(got, ref, atol=ATOL, rtol=RTOL):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref)
+    bound = atol + rtol * np.abs(ref)
+    worst = np.unravel_index(np.argmax(err - bound), err.shape)
+    assert np.all(err <= bound), f"max excess at {worst}: got {got[worst]} ref {ref[worst]} (max abs err {err.max():.3e})"
+
+
+def bf16(bits, dev):
+    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+
+
+def test_library_is_native():
+    from starkv_b200 import _lib
+    _lib.check_abi()
+    assert os.path.exists(_lib.LIB_PATH)
+
+
+@pytest.mark.parametrize("name", ["decode_bf16_mha.npz", "decode_bf16_ragged.npz", "decode_bf16_gqa.npz"])
+def test_bf16_decode_golden(golden_dir, name):
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    dev = cuda()
+    c = dict(np.load(os.path.join(golden_dir, name)))
+    out = paged_starkv_decode(bf16(c["query"], dev), bf16(c["cache"], dev),
+                              torch.from_numpy(c["block_table"]).to(dev), torch.from_numpy(c["seq_lens"]).to(dev),
+                              int(c["seq_lens"].max()), bf16(c["k_up"], dev), torch.from_numpy(c["k_ranks"]).to(dev),
+                              torch.from_numpy(c["k_head_offsets"]).to(dev), int(c["k_width"]),
+                              bf16(c["v_up_by_q"], dev), bf16(c["cos_sin"], dev), float(c["scale"]))
+    assert out.dtype == torch.bfloat16
+    assert_close(out.float().cpu().numpy(), c["out_ref_fp32"])
+
+
+@pytest.mark.parametrize("path", sorted(p for p in os.listdir(os.path.join(os.path.dirname(__file__), "golden"))
+                                        if p.startswith("pack_")))
+def test_pack_kv_golden_bit_exact(golden_dir, path):
+    from starkv_b200.kernels import paged_quant as pq
+    dev = cuda()
+    c = dict(np.load(os.path.join(golden_dir, path)))
+    ranks = [int(r) for r in c["ranks"]]
+    _, offsets, W = O.k_layout(ranks)
+    row = pq.QuantRow(W, len(ranks), int(c["v_rank"]))
+    T = c["rows"].shape[0]
+    cache = torch.zeros(T + 16, 1, row.nbytes, dtype=torch.uint8, device=dev)   # block_size 1: slot == block
+    slots = torch.arange(T, dtype=torch.int64, device=dev) + 3
+    nouts, _, _ = pq.k_tables(ranks, dev)
+    pq.pack_kv(bf16(c["k_codes"], dev), bf16(c["v_codes"], dev), cache, slots, row,
+               torch.tensor(ranks, dtype=torch.int32, device=dev), torch.tensor(offsets, dtype=torch.int32, device=dev),
+               nouts)
+    got = cache[3:3 + T, 0].cpu().numpy()
+    np.testing.assert_array_equal(got, c["rows"])
+    assert not cache[:3].any() and not cache[3 + T:].any()
+
+
+@pytest.mark.parametrize("name", ["decode_quant.npz", "decode_quant_b.npz"])
+def test_quant_decode_golden(golden_dir, name):
+    from starkv_b200.kernels import paged_quant as pq
+    dev = cuda()
+    c = dict(np.load(os.path.join(golden_dir, name)))
+    ranks = [int(r) for r in c["k_ranks"]]
+    _, _, W = O.k_layout(ranks)
+    row = pq.QuantRow(W, len(ranks), int(c["v_rank"]))
+    nouts, hol, tiles = pq.k_tables(ranks, dev)
+    out = pq.paged_quant_decode(bf16(c["query"], dev), torch.from_numpy(c["cache"]).to(dev),
+                                torch.from_numpy(c["block_table"]).to(dev), torch.from_numpy(c["seq_lens"]).to(dev),
+                                int(c["seq_lens"].max()), row, bf16(c["k_up"], dev), hol, tiles,
+                                bf16(c["v_up_by_q"], dev), bf16(c["cos_sin"], dev), float(c["scale"]))
+    assert_close(out.float().cpu().numpy(), c["out_ref_fp32"])
+
+
+def _oracle_bf16(layer, seqs):
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    outs = []
+    for b in seqs:
+        from starkv_b200.workload import gather_rows
+        rows = gather_rows(layer, b).float().numpy()
+        outs.append(O.attend_one(f(layer.query[b]), rows[:, :layer.k_width], rows[:, layer.k_width:],
+                                 f(layer.k_up), layer.ranks, layer.offsets,
+                                 layer.num_heads // len(layer.ranks), f(layer.v_up_by_q), f(layer.cos_sin_cache),
+                                 layer.scale))
+    return np.stack(outs)
+
+
+def _oracle_quant(layer, seqs):
+    from starkv_b200.workload import gather_rows
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    row = O.QuantRow(layer.k_width, len(layer.ranks), layer.v_rank)
+    outs = []
+    for b in seqs:
+        rows = gather_rows(layer, b).numpy()
+        kd, vd = O.unpack_rows(rows, row, layer.ranks)
+        outs.append(O.attend_one(f(layer.query[b]), kd, vd, f(layer.k_up), layer.ranks, layer.offsets, 1,
+                                 f(layer.v_up_by_q), f(layer.cos_sin_cache), layer.scale))
+    return np.stack(outs)
+
+
+EDGE_LENS = [1, 15, 16, 17, 127, 128, 129, 300, 1000, 2049]
+
+
+def test_bf16_edge_lengths_vs_oracle():
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer
+    dev = cuda()
+    L = make_layer(EDGE_LENS, num_heads=32, seed=3, device=dev)
+    out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
+                              L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale)
+    assert_close(out.float().cpu().numpy(), _oracle_bf16(L, range(L.n)))
+
+
+def test_bf16_gqa_and_skewed_ranks_vs_oracle():
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer
+    dev = cuda()
+    L = make_layer([5, 200, 700], num_heads=16, num_kv_heads=8, seed=5, device=dev, skewed=True,
+                   max_seq_len=1024)
+    out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
+                              L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale)
+    assert_close(out.float().cpu().numpy(), _oracle_bf16(L, range(L.n)))
+
+
+def test_quant_edge_lengths_vs_oracle_and_pack_bits():
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.workload import gather_rows, make_layer
+    dev = cuda()
+    L = make_layer(EDGE_LENS, num_heads=32, quant=True, seed=4, device=dev)
+    out = pq.paged_quant_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.row, L.k_up,
+                                L.head_of_lane, L.k_tiles, L.v_up_by_q, L.cos_sin_cache, L.scale)
+    assert_close(out.float().cpu().numpy(), _oracle_quant(L, range(L.n)))
+
+
+def test_quant_pack_matches_oracle_bits():
+    """GPU packer == CPU oracle packer on random codes, byte for byte (config-3 geometry)."""
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.workload import sample_ranks
+    dev = cuda()
+    ranks, rv = sample_ranks(32, 0)
+    _, offsets, W = O.k_layout(ranks)
+    row = pq.QuantRow(W, 32, rv)
+    g = torch.Generator(device=dev).manual_seed(9)
+    T = 512
+    k = (torch.randn(T, W, generator=g, device=dev) * 1.7).to(torch.bfloat16)
+    v = (torch.randn(T, rv, generator=g, device=dev) * 2.3).to(torch.bfloat16)
+    for r, o, w in zip(ranks, offsets, [O.align_up(r, 16) for r in ranks]):
+        k[:, o + r:o + w] = 0
+    cache = torch.zeros(T // 16, 16, row.nbytes, dtype=torch.uint8, device=dev)
+    nouts, _, _ = pq.k_tables(ranks, dev)
+    pq.pack_kv(k, v, cache, torch.arange(T, device=dev, dtype=torch.int32), row,
+               torch.tensor(ranks, dtype=torch.int32, device=dev), torch.tensor(offsets, dtype=torch.int32, device=dev),
+               nouts)
+    ref = O.pack_rows(k.float().cpu().numpy(), v.float().cpu().numpy(), O.QuantRow(W, 32, rv), ranks)
+    np.testing.assert_array_equal(cache.view(T, row.nbytes).cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_full_size_config_sampled(quant):
+    """Configs 2/3 at full size; every sequence checked by a size-independent
+    property (finite, bounded by the V lift), three sampled sequences by the oracle."""
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer
+    dev = cuda()
+    n, Lx = (64, 16384) if quant else (64, 8192)
+    L = make_layer([Lx] * n, num_heads=32, quant=quant, seed=0, device=dev)
+    if quant:
+        out = pq.paged_quant_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.row, L.k_up,
+                                    L.head_of_lane, L.k_tiles, L.v_up_by_q, L.cos_sin_cache, L.scale)
+        ref = _oracle_quant(L, [0, 31, 63])
+    else:
+        out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
+                                  L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale)
+        ref = _oracle_bf16(L, [0, 31, 63])
+    o = out.float().cpu().numpy()
+    assert np.isfinite(o).all()
+    assert_close(o[[0, 31, 63]], ref)
+    del L
+    torch.cuda.empty_cache()
+
+
+def test_bad_block_id_recorded_not_faulting():
+    """An out-of-range block id is skipped (null block read instead) and reported
+    in the workspace status word; the context stays usable."""
+    from starkv_b200 import workspace
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer
+    dev = cuda()
+    L = make_layer([40, 40], num_heads=32, seed=6, device=dev)
+    bt = L.block_table.clone()
+    bt[1, 1] = L.kv_cache.shape[0] + 1000
+    ws = workspace.reserve(dev, L.n, 32, 32, L.k_width, L.v_rank, L.max_seq_len)
+    workspace.read_status(ws, reset=True)
+    paged_starkv_decode(L.query, L.kv_cache, bt, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
+                        L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale, ws=ws)
+    assert workspace.read_status(ws, reset=True) == 105
+    torch.cuda.synchronize()
+    # the next call runs cleanly
+    out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
+                              L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale, ws=ws)
+    assert workspace.read_status(ws) == 0
+    assert_close(out.float().cpu().numpy(), _oracle_bf16(L, range(L.n)))
