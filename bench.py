@@ -96,9 +96,10 @@ def shard_layer_spec(ranks, world, rank):
     return lpt_shard(ranks, world)[rank]
 
 
-def build_layer(quant: bool, world: int, rank: int, device):
+def build_layer(quant: bool, world: int, rank: int, device, batch=None, context=None):
     from starkv_b200.workload import make_layer, sample_ranks
     n, L = (64, 16384) if quant else (64, 8192)
+    n, L = batch or n, context or L
     ranks, rv = sample_ranks(32, 0)
     heads = list(range(32)) if world == 1 else shard_layer_spec(ranks, world, rank)
     local = [ranks[h] for h in heads]
@@ -283,17 +284,24 @@ def ours(args):
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
     hbm_peak, tf_peak, peak_kind = peaks()
     res = {}
-    for quant in (False, True):
-        layer, heads = build_layer(quant, world, rank, device)
+    cases = {"c2": (False,), "c3": (True,), "both": (False, True)}[args.case]
+    for quant in cases:
+        layer, heads = build_layer(quant, world, rank, device, args.batch, args.context)
         ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on)
         res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
                           d2h=d2h, alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
                           roof=roofline_for(layer, per_kernel, hbm_peak))
         del layer
         torch.cuda.empty_cache()
-    if rank == 0:
+    if rank == 0 and args.case != "both":
+        # single-configuration run (profiling): short line, no baselines
+        r = res[cases[0]]
+        print(json.dumps({"case": args.case, "batch": r["layer"].n, "context": r["layer"].seq_lens_host[0],
+                          "ms_per_step": round(r["ms"], 4), "kernel_ms": r["roof"]["kernel_ms"],
+                          "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1)}), flush=True)
+    elif rank == 0:
         b = res[False]
-        n = b["layer"].n if False else 64
+        n = b["layer"].n
         cpu_rate, cpu_desc = (None, None)
         if world == 1:
             cpu_rate, cpu_desc = cpu_sample_time(False)
@@ -318,7 +326,7 @@ def ours(args):
             "gpu_launches": 5 * args.steps,
             "clocks": b["clocks"],
             "q32": {"workload": "config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
-                    "value": round(64 / (q["ms"] * 1e-3), 1), "unit": UNIT, "ms_per_step": round(q["ms"], 4),
+                    "value": round(q["layer"].n / (q["ms"] * 1e-3), 1), "unit": UNIT, "ms_per_step": round(q["ms"], 4),
                     "us_per_layer": round(q["ms"] * 1e3, 1),
                     "hbm_gbs": round(q["alg"] / (q["ms"] * 1e-3) / 1e9, 1),
                     "hbm_frac_step": round(q["alg"] / (q["ms"] * 1e-3) / 1e9 / hbm_peak, 4),
@@ -362,6 +370,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--case", default="both", choices=["both", "c2", "c3"],
+                    help="c2 / c3 alone: one configuration, short output (profiling)")
+    ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling small cases)")
+    ap.add_argument("--context", type=int, default=None, help="override the context (profiling small cases)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":

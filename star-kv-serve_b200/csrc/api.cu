@@ -98,9 +98,10 @@ Workspace workspace_layout(int n, int num_heads, int num_kv_heads, int k_width, 
   w.cs = off; off = align256(off + (size_t)w.l_pad * 128 * 2);
   w.e16 = off; off = align256(off + (size_t)n * num_heads * w.l_pad * 2);
   w.m_tile = off; off = align256(off + (size_t)n * num_heads * w.n_tiles * 4);
-  w.l_tile = off; off = align256(off + (size_t)n * num_heads * w.n_tiles * 4);
+  w.l_seq = off; off = align256(off + (size_t)n * num_heads * 4);
   w.m_seq = off; off = align256(off + (size_t)n * num_heads * 4);
-  w.pv = off; off = align256(off + (size_t)n * num_heads * v_rank * 4);
+  w.pv_stride = (v_rank + 63) / 64 * 64;
+  w.pv = off; off = align256(off + (size_t)n * num_heads * w.pv_stride * 4);
   w.total = off;
   return w;
 }
@@ -149,7 +150,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   __half* cs16 = reinterpret_cast<__half*>(W + ws.cs);
   __half* e16 = reinterpret_cast<__half*>(W + ws.e16);
   float* m_tile = reinterpret_cast<float*>(W + ws.m_tile);
-  float* l_tile = reinterpret_cast<float*>(W + ws.l_tile);
+  float* l_seq = reinterpret_cast<float*>(W + ws.l_seq);
   float* m_seq = reinterpret_cast<float*>(W + ws.m_seq);
   float* pv = reinterpret_cast<float*>(W + ws.pv);
 
@@ -201,8 +202,8 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   fp.k_width = a->k_width; fp.head_dim = a->head_dim; fp.scale = a->scale; fp.ab = ab;
   fp.cs = a->cos_sin_cache; fp.cs_s0 = a->cs_stride[0]; fp.cs_s1 = a->cs_stride[1]; fp.cs_dtype = a->cs_dtype;
   fp.cs_rows = a->cs_rows; fp.cs16 = cs16; fp.l_pad = ws.l_pad; fp.max_seq_len = a->max_seq_len;
-  fp.m_seq = m_seq; fp.m_count = a->n * a->num_heads;
-  fp.pv = pv; fp.pv_count = (int64_t)a->n * a->num_heads * a->v_rank;
+  fp.m_seq = m_seq; fp.l_seq = l_seq; fp.m_count = a->n * a->num_heads;
+  fp.pv = pv; fp.pv_count = (int64_t)a->n * a->num_heads * ws.pv_stride;
   fp.status = status;
   cudaEvent_t* pev = nullptr;
   if (g_prof.on && g_prof.calls < g_prof.max_calls) pev = g_prof.ev + 5 * g_prof.calls++;
@@ -225,7 +226,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
     sp.ks_boxes = (a->ks_off + 4 * a->num_kv_heads - sp.ks_x0 + 127) / 128;
     if (sp.ks_boxes > 3) return STARKV_EINVAL;
   }
-  sp.e16 = e16; sp.m_tile = m_tile; sp.l_tile = l_tile; sp.m_seq = m_seq;
+  sp.e16 = e16; sp.m_tile = m_tile; sp.m_seq = m_seq;
   sp.l_pad = ws.l_pad; sp.n_tiles = ws.n_tiles; sp.status = status;
   if ((st = launch_scores(quant, tm_cs, tm_ab, tm_codes, tm_wide, sp, dev.sms, stream))) return st;
   if (pev) cudaEventRecord(pev[2], stream);
@@ -254,27 +255,36 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
     pp.mt_per_range = mtpr;
     if (pv_smem_bytes(quant, pp) <= 227 * 1024 && mtpr >= 1) {
       // at least two pipeline stages
-      const int stage = (quant ? pp.v_boxes * 2048 + mtpr * 4096 : mtpr * 4096) + 2 * pp.nh * 32;
+      const int stage = (quant ? pp.v_boxes * 2048 + mtpr * 4096 : mtpr * 4096) + 2 * pp.nh * 32 +
+                        ((a->num_heads * 32 + 127) & ~127);
       if (2 * ((stage + 1023) & ~1023) <= 200 * 1024) break;
     }
     if (--mtpr < 1) return STARKV_EINVAL;
   }
   pp.n_ranges = (pp.n_mtiles + mtpr - 1) / mtpr;
   pp.mt_per_range = (pp.n_mtiles + pp.n_ranges - 1) / pp.n_ranges;   // balance the ranges
-  pp.e16 = e16; pp.m_tile = m_tile; pp.m_seq = m_seq; pp.pv = pv;
+  pp.e16 = e16; pp.m_tile = m_tile; pp.m_seq = m_seq; pp.l_seq = l_seq; pp.pv = pv; pp.pv_stride = ws.pv_stride;
   pp.l_pad = ws.l_pad; pp.n_tiles = ws.n_tiles; pp.status = status;
-  if ((st = launch_pv(quant, tm_wide, pp, dev.sms, stream))) return st;
+  CUtensorMap tm_e;
+  {
+    const uint64_t dims[2] = {(uint64_t)ws.l_pad, (uint64_t)a->n * a->num_heads};
+    const uint64_t str[1] = {(uint64_t)ws.l_pad * 2};
+    const uint32_t box[2] = {16, (uint32_t)a->num_heads};
+    if ((st = make_map(&tm_e, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e16, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
+  }
+  if ((st = launch_pv(quant, tm_wide, tm_e, pp, dev.sms, stream))) return st;
   if (pev) cudaEventRecord(pev[3], stream);
 
   // ---- lift ----
   LiftParams lp{};
-  lp.pv = pv; lp.m_tile = m_tile; lp.l_tile = l_tile; lp.m_seq = m_seq;
+  lp.pv = pv; lp.pv_stride = ws.pv_stride; lp.l_seq = l_seq;
   lp.v_up = a->v_up_by_q; lp.vu_s0 = a->v_up_stride[0]; lp.vu_s1 = a->v_up_stride[1]; lp.vu_s2 = a->v_up_stride[2];
   lp.v_up_dtype = a->v_up_dtype;
   lp.out = a->out; lp.o_s0 = a->out_stride[0]; lp.o_s1 = a->out_stride[1]; lp.o_s2 = a->out_stride[2];
   lp.out_dtype = a->out_dtype;
-  lp.seq_lens = a->seq_lens; lp.n = a->n; lp.num_heads = a->num_heads; lp.v_rank = a->v_rank;
-  lp.head_dim = a->head_dim; lp.n_tiles = ws.n_tiles; lp.max_seq_len = a->max_seq_len;
+  lp.n = a->n; lp.num_heads = a->num_heads; lp.v_rank = a->v_rank;
+  lp.head_dim = a->head_dim;
   st = launch_lift(lp, stream);
   if (pev) cudaEventRecord(pev[4], stream);
   return st;

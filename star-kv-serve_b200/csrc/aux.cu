@@ -14,53 +14,78 @@ namespace starkv {
 // fold + rotary table + init (one launch)
 // ---------------------------------------------------------------------------
 
-constexpr int kFoldLanes = 4;   // K lanes per 256-thread block (64 threads each)
+constexpr int kFoldLanes = 16;   // K lanes per 128-thread block (8 threads x 8 values each)
 
-__global__ void __launch_bounds__(256) fold_kernel(const FoldParams p, int n_fold_blocks, int n_cs_blocks) {
+template <class TQ, class TU>
+__global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fold_blocks, int n_cs_blocks) {
   const int bid = blockIdx.x;
   if (bid < n_fold_blocks) {
-    // block -> (b, j, 4 lanes); thread -> (lane, i in 0..63)
+    // block -> (b, j, 16 lanes); thread -> (lane, 8 consecutive i of 0..63)
+    __shared__ int head_of[kFoldLanes];
     const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
     const int bj = bid / lanes_per_seq;
-    const int r = (bid % lanes_per_seq) * kFoldLanes + (threadIdx.x >> 6);
-    const int i = threadIdx.x & 63;
-    const int b = bj / p.group, j = bj % p.group;
-    if (r >= p.k_width) return;
-    int head = -1;
-    bool live = true;
-    if (p.head_of_lane) {
-      head = p.head_of_lane[r];
-    } else {
-      for (int h = 0; h < p.num_kv_heads; ++h) {
-        const int off = p.k_head_offsets[h], rk = p.k_ranks[h];
-        const int w = (rk + 15) & ~15;
-        if (r >= off && r < off + w) {
-          head = h;
-          live = (r - off) < rk;
-          break;
+    const int r0 = (bid % lanes_per_seq) * kFoldLanes;
+    if (threadIdx.x < kFoldLanes) {
+      const int r = r0 + threadIdx.x;
+      int head = -1;
+      if (r < p.k_width) {
+        if (p.head_of_lane) {
+          head = p.head_of_lane[r];
+          if (head < 0 || head >= p.num_kv_heads) {
+            record_status(p.status, STARKV_EBOUNDS);
+            head = -1;
+          }
+        } else {
+          for (int h = 0; h < p.num_kv_heads; ++h) {
+            const int off = p.k_head_offsets[h], rk = p.k_ranks[h];
+            if (r >= off && r < off + ((rk + 15) & ~15)) {
+              head = (r - off) < rk ? h : -1;   // lanes past the rank get zero rows
+              break;
+            }
+          }
         }
+      }
+      head_of[threadIdx.x] = head;
+    }
+    __syncthreads();
+    const int lr = threadIdx.x >> 3, i0 = (threadIdx.x & 7) * 8;
+    const int r = r0 + lr;
+    if (r >= p.k_width) return;
+    const int b = bj / p.group, j = bj % p.group;
+    const int head = head_of[lr];
+    __half av[8], bv[8];
+    if (head < 0) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) av[k] = bv[k] = __float2half_rn(0.f);
+    } else {
+      const int hq = head * p.group + j;
+      const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)hq * p.q_s1;
+      const TU* up = reinterpret_cast<const TU*>(p.k_up) + (int64_t)r * p.ku_s0;
+      TQ q0[8], q1[8];
+      TU u0[8], u1[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {   // all loads first, so they are in flight together
+        const int i = i0 + k;
+        q0[k] = qp[(int64_t)i * p.q_s2];
+        q1[k] = qp[(int64_t)(i + 64) * p.q_s2];
+        u0[k] = up[(int64_t)i * p.ku_s1];
+        u1[k] = up[(int64_t)(i + 64) * p.ku_s1];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float a0 = to_f32(q0[k]), a1 = to_f32(q1[k]), w0 = to_f32(u0[k]), w1 = to_f32(u1[k]);
+        av[k] = __float2half_rn((a0 * w0 + a1 * w1) * p.scale);
+        bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
       }
     }
     __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
-    if (head < 0 || head >= p.num_kv_heads || !live) {
-      if (head >= p.num_kv_heads) record_status(p.status, STARKV_EBOUNDS);
-      dst[i] = __float2half_rn(0.f);
-      dst[i + 64] = __float2half_rn(0.f);
-      return;
-    }
-    const int hq = head * p.group + j;
-    const int64_t qo = (int64_t)b * p.q_s0 + (int64_t)hq * p.q_s1;
-    const float q0 = load_elem(p.q, qo + (int64_t)i * p.q_s2, p.q_dtype);
-    const float q1 = load_elem(p.q, qo + (int64_t)(i + 64) * p.q_s2, p.q_dtype);
-    const float u0 = load_elem(p.k_up, (int64_t)r * p.ku_s0 + (int64_t)i * p.ku_s1, p.k_up_dtype);
-    const float u1 = load_elem(p.k_up, (int64_t)r * p.ku_s0 + (int64_t)(i + 64) * p.ku_s1, p.k_up_dtype);
-    dst[i] = __float2half_rn((q0 * u0 + q1 * u1) * p.scale);
-    dst[i + 64] = __float2half_rn((q1 * u0 - q0 * u1) * p.scale);
+    *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
+    *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
     return;
   }
   if (bid < n_fold_blocks + n_cs_blocks) {
     // rotary table rows -> f16, zero past the table / max_seq_len
-    const int64_t e = (int64_t)(bid - n_fold_blocks) * 256 + threadIdx.x;
+    const int64_t e = (int64_t)(bid - n_fold_blocks) * 128 + threadIdx.x;
     const int64_t row = e >> 7;
     const int col = (int)(e & 127);
     if (row >= p.l_pad) return;
@@ -70,9 +95,12 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p, int n_fol
     return;
   }
   // init: sequence max = -inf, pv = 0
-  const int64_t t = (int64_t)(bid - n_fold_blocks - n_cs_blocks) * 256 + threadIdx.x;
-  const int64_t stride = (int64_t)(gridDim.x - n_fold_blocks - n_cs_blocks) * 256;
-  for (int64_t k = t; k < p.m_count; k += stride) p.m_seq[k] = -INFINITY;
+  const int64_t t = (int64_t)(bid - n_fold_blocks - n_cs_blocks) * 128 + threadIdx.x;
+  const int64_t stride = (int64_t)(gridDim.x - n_fold_blocks - n_cs_blocks) * 128;
+  for (int64_t k = t; k < p.m_count; k += stride) {
+    p.m_seq[k] = -INFINITY;
+    p.l_seq[k] = 0.f;
+  }
   float4* pv4 = reinterpret_cast<float4*>(p.pv);
   const int64_t n4 = p.pv_count >> 2;
   for (int64_t k = t; k < n4; k += stride) pv4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -83,72 +111,155 @@ int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream) {
   (void)quant;
   const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
   const int n_fold = p.n * p.group * lanes_per_seq;
-  const int n_cs = (int)(((int64_t)p.l_pad * 128 + 255) / 256);
-  const int n_init = 148;
-  fold_kernel<<<n_fold + n_cs + n_init, 256, 0, stream>>>(p, n_fold, n_cs);
+  const int n_cs = (int)(((int64_t)p.l_pad * 128 + 127) / 128);
+  const int n_init = 296;
+  with_float_type(p.q_dtype, [&](auto tq) {
+    with_float_type(p.k_up_dtype, [&](auto tu) {
+      fold_kernel<decltype(tq), decltype(tu)><<<n_fold + n_cs + n_init, 128, 0, stream>>>(p, n_fold, n_cs);
+    });
+  });
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 
 // ---------------------------------------------------------------------------
 // lift: out[b, h, :] = (pv[b, h, :] / l[b, h]) . v_up_by_q[h]
+//
+// Per head a [n x rv] x [rv x 128] product on mma.sync m16n8k16 (bf16 in, f32
+// accumulate). The normalised pv row is split into bf16 hi + lo parts (two MMAs)
+// so the product keeps ~16 mantissa bits, well past the reference's bf16 cast
+// (paged_decode.py:225). Block = (head, 32 output columns, 64 sequences); warp w
+// owns sequences [16w, 16w+16); v_up_by_q tiles are staged through shared memory
+// and read with ldmatrix.trans.
 // ---------------------------------------------------------------------------
 
-constexpr int kLiftB = 16;     // sequences per block
-constexpr int kLiftV = 32;     // V channels staged per step
+constexpr int kLiftBT = 64;    // sequences per block
+constexpr int kLiftVT = 64;    // V channels staged per step
+constexpr int kLiftLd = 40;    // staged row stride (elements): 80 B, conflict-free ldmatrix
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <class TV>
 __global__ void __launch_bounds__(128) lift_kernel(const LiftParams p) {
   const int h = blockIdx.x;
-  const int b0 = blockIdx.y * kLiftB;
-  const int d = threadIdx.x;
-  __shared__ float inv_l[kLiftB];
-  __shared__ float pvs[kLiftB][kLiftV];
-  if (threadIdx.x < kLiftB) {
-    const int b = b0 + threadIdx.x;
-    float l = 0.f;
-    if (b < p.n) {
-      const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
-      const int nt = (L + 127) >> 7;
-      const float M = p.m_seq[(int64_t)b * p.num_heads + h];
-      const int64_t base = ((int64_t)b * p.num_heads + h) * p.n_tiles;
-      for (int t = 0; t < nt; ++t) l += p.l_tile[base + t] * __expf(p.m_tile[base + t] - M);
-    }
-    inv_l[threadIdx.x] = l > 0.f ? 1.f / l : 0.f;   // empty sequence -> 0, as the reference
+  const int d0 = blockIdx.y * 32;
+  const int b0 = blockIdx.z * kLiftBT;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  __shared__ float inv_l[kLiftBT];
+  __shared__ __align__(16) float pvt[kLiftBT][kLiftVT + 4];          // [b][v], padded rows
+  __shared__ __align__(16) __nv_bfloat16 vt[kLiftVT][kLiftLd];       // [v][d]
+  if (tid < kLiftBT) {
+    const int b = b0 + tid;
+    const float l = b < p.n ? p.l_seq[(int64_t)b * p.num_heads + h] : 0.f;
+    inv_l[tid] = l > 0.f ? 1.f / l : 0.f;   // empty sequence -> 0, as the reference
   }
-  float acc[kLiftB];
+  // per-thread share of one staged step: 8 x float4 of pv, 16 bf16 of v_up
+  float4 rp[8];
+  TV rv[16];
+  int vnext = 0;
+  auto fetch = [&](int v0) {
+    vnext = v0;
 #pragma unroll
-  for (int i = 0; i < kLiftB; ++i) acc[i] = 0.f;
-  for (int v0 = 0; v0 < p.v_rank; v0 += kLiftV) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < kLiftB * kLiftV; e += blockDim.x) {
-      const int bb = e / kLiftV, vv = e % kLiftV;
-      const int b = b0 + bb, v = v0 + vv;
-      pvs[bb][vv] = (b < p.n && v < p.v_rank) ? p.pv[((int64_t)b * p.num_heads + h) * p.v_rank + v] : 0.f;
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + 128 * i;           // 1024 float4 = 64 rows x 16
+      const int bb = e >> 4, vq = (e & 15) * 4;
+      const int b = min(b0 + bb, p.n - 1);
+      rp[i] = *reinterpret_cast<const float4*>(p.pv + ((int64_t)b * p.num_heads + h) * p.pv_stride + v0 + vq);
     }
-    __syncthreads();
-    if (d < p.head_dim) {
-      const int vmax = min(kLiftV, p.v_rank - v0);
-      for (int vv = 0; vv < vmax; ++vv) {
-        const float w = load_elem(p.v_up, (int64_t)h * p.vu_s0 + (int64_t)(v0 + vv) * p.vu_s1 + (int64_t)d * p.vu_s2,
-                                  p.v_up_dtype);
 #pragma unroll
-        for (int i = 0; i < kLiftB; ++i) acc[i] += pvs[i][vv] * w;
+    for (int i = 0; i < 16; ++i) {
+      const int e = tid + 128 * i;           // 2048 = 64 v x 32 d
+      const int vv = e >> 5, dd = e & 31;
+      const int v = v0 + vv;
+      const int64_t o = (int64_t)h * p.vu_s0 + (int64_t)min(v, p.v_rank - 1) * p.vu_s1 +
+                        (int64_t)min(d0 + dd, p.head_dim - 1) * p.vu_s2;
+      rv[i] = reinterpret_cast<const TV*>(p.v_up)[o];   // raw load; range masked at the stash
+    }
+  };
+  int vbase = 0;   // first V channel of the step held in rv
+  auto stash = [&]() {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + 128 * i;
+      *reinterpret_cast<float4*>(&pvt[e >> 4][(e & 15) * 4]) = rp[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = tid + 128 * i;
+      const int vv = e >> 5, dd = e & 31;
+      const bool in = (vbase + vv < p.v_rank) && (d0 + dd < p.head_dim);
+      vt[vv][dd] = __float2bfloat16_rn(in ? to_f32(rv[i]) : 0.f);
+    }
+  };
+  const int rA = 16 * warp + g, rB = rA + 8;   // rows within the block's 64 sequences
+  float acc[4][4] = {};
+  fetch(0);
+  __syncthreads();   // inv_l ready
+  const float sA = inv_l[rA], sB = inv_l[rB];
+  for (int v0 = 0; v0 < p.v_rank; v0 += kLiftVT) {
+    __syncthreads();
+    vbase = vnext;
+    stash();
+    __syncthreads();
+    if (v0 + kLiftVT < p.v_rank) fetch(v0 + kLiftVT);   // next step's loads overlap this step's MMAs
+#pragma unroll
+    for (int ks = 0; ks < kLiftVT / 16; ++ks) {
+      const int c0 = ks * 16 + 2 * t, c1 = c0 + 8;
+      const float2 xa0 = *reinterpret_cast<const float2*>(&pvt[rA][c0]);
+      const float2 xb0 = *reinterpret_cast<const float2*>(&pvt[rB][c0]);
+      const float2 xa1 = *reinterpret_cast<const float2*>(&pvt[rA][c1]);
+      const float2 xb1 = *reinterpret_cast<const float2*>(&pvt[rB][c1]);
+      const float x[8] = {xa0.x * sA, xa0.y * sA, xb0.x * sB, xb0.y * sB,
+                          xa1.x * sA, xa1.y * sA, xb1.x * sB, xb1.y * sB};
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float e0 = x[2 * j], e1 = x[2 * j + 1];
+        const float h0 = __bfloat162float(__float2bfloat16_rn(e0)), h1 = __bfloat162float(__float2bfloat16_rn(e1));
+        hi[j] = pack_bf16x2(h0, h1);
+        lo[j] = pack_bf16x2(e0 - h0, e1 - h1);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        // B fragment (k = v, n = d) from the staged [v][d] tile, transposed by ldmatrix
+        uint32_t b0r, b1r;
+        const __nv_bfloat16* rowp = &vt[ks * 16 + (lane & 15)][nt * 8];
+        asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+                     : "=r"(b0r), "=r"(b1r)
+                     : "r"(smem_u32(rowp)));
+        mma_bf16_16816(acc[nt], hi, b0r, b1r);
+        mma_bf16_16816(acc[nt], lo, b0r, b1r);
       }
     }
   }
-  __syncthreads();
-  if (d < p.head_dim) {
-    for (int i = 0; i < kLiftB; ++i) {
-      const int b = b0 + i;
-      if (b < p.n)
-        store_elem(p.out, (int64_t)b * p.o_s0 + (int64_t)h * p.o_s1 + (int64_t)d * p.o_s2, p.out_dtype,
-                   acc[i] * inv_l[i]);
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int d = d0 + nt * 8 + 2 * t;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int b = b0 + (j ? rB : rA);
+      if (b >= p.n) continue;
+      const int64_t o = (int64_t)b * p.o_s0 + (int64_t)h * p.o_s1;
+      if (d < p.head_dim) store_elem(p.out, o + (int64_t)d * p.o_s2, p.out_dtype, acc[nt][2 * j]);
+      if (d + 1 < p.head_dim) store_elem(p.out, o + (int64_t)(d + 1) * p.o_s2, p.out_dtype, acc[nt][2 * j + 1]);
     }
   }
 }
 
 int launch_lift(const LiftParams& p, cudaStream_t stream) {
-  dim3 grid(p.num_heads, (p.n + kLiftB - 1) / kLiftB);
-  lift_kernel<<<grid, 128, 0, stream>>>(p);
+  dim3 grid(p.num_heads, (p.head_dim + 31) / 32, (p.n + kLiftBT - 1) / kLiftBT);
+  with_float_type(p.v_up_dtype, [&](auto tv) { lift_kernel<decltype(tv)><<<grid, 128, 0, stream>>>(p); });
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 

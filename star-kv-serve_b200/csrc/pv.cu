@@ -43,6 +43,7 @@ struct PvCtl {
 struct PvLayout {
   int v_bytes;      // TMA tile bytes per stage
   int a_bytes;      // dequantized A tiles per stage (3.2-bit)
+  int e_bytes;      // TMA tile of e16 (heads x 16 tokens) per stage
   int p_bytes;      // P operand(s) per stage
   int stage_bytes;  // all of the above, 1024-aligned
   int stages;
@@ -53,8 +54,9 @@ __host__ __device__ inline PvLayout pv_layout(bool quant, const PvParams& p) {
   PvLayout L;
   L.v_bytes = quant ? p.v_boxes * 2048 : p.mt_per_range * 4096;
   L.a_bytes = quant ? p.mt_per_range * 4096 : 0;
+  L.e_bytes = (p.num_heads * 32 + 127) & ~127;
   L.p_bytes = (quant ? 2 : 1) * p.nh * 32;
-  L.stage_bytes = (L.v_bytes + L.a_bytes + L.p_bytes + 1023) & ~1023;
+  L.stage_bytes = (L.v_bytes + L.a_bytes + L.e_bytes + L.p_bytes + 1023) & ~1023;
   int s = (200 * 1024) / L.stage_bytes;
   L.stages = s > kMaxStages ? kMaxStages : s;
   L.total = L.stages * L.stage_bytes + (int)sizeof(PvCtl) + 1024 + 64;
@@ -119,7 +121,8 @@ size_t pv_smem_bytes(bool quant, const PvParams& p) {
 }
 
 template <bool QUANT>
-__global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUtensorMap tm_v, const PvParams p) {
+__global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUtensorMap tm_v,
+                                                    const __grid_constant__ CUtensorMap tm_e, const PvParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const PvLayout LY = pv_layout(QUANT, p);
@@ -164,6 +167,8 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
     // ================= TMA producer =================
     if (lane == 0) {
       tma_prefetch(&tm_v);
+      tma_prefetch(&tm_e);
+      const int e_bytes = p.num_heads * 32;
       uint32_t it = 0;
       int u = u_begin;
       SubItem si;
@@ -184,16 +189,18 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
           const int slot = t % p.block_size;
           uint8_t* st = smem + s * LY.stage_bytes;
           if (QUANT) {
-            mbar_arrive_expect_tx(&ctl->vfull[s], p.v_boxes * 2048);
+            mbar_arrive_expect_tx(&ctl->vfull[s], p.v_boxes * 2048 + e_bytes);
             for (int jb = 0; jb < p.v_boxes; ++jb)
               tma_load_3d(st + jb * 2048, &tm_v, &ctl->vfull[s], p.vx0 + 128 * jb, slot, blk);
           } else {
-            mbar_arrive_expect_tx(&ctl->vfull[s], (mt1 - mt0) * 4096);
+            mbar_arrive_expect_tx(&ctl->vfull[s], (mt1 - mt0) * 4096 + e_bytes);
             for (int m = mt0; m < mt1; ++m)
               for (int i = 0; i < 2; ++i)
                 tma_load_3d(st + (m - mt0) * 4096 + i * 2048, &tm_v, &ctl->vfull[s], p.k_width + m * 128 + 64 * i,
                             slot, blk);
           }
+          // e16 rows of this sequence's heads for the page's 16 tokens
+          tma_load_2d(st + LY.v_bytes + LY.a_bytes, &tm_e, &ctl->vfull[s], t, si.b * p.num_heads);
         }
       }
     }
@@ -216,7 +223,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
           if (!mbar_wait(&ctl->pfull[s], (it / S) & 1, abort_flag, p.status)) break;
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * LY.stage_bytes);
-          const uint32_t pbase = st + LY.v_bytes + LY.a_bytes;
+          const uint32_t pbase = st + LY.v_bytes + LY.a_bytes + LY.e_bytes;
           for (int m = 0; m < nmt; ++m) {
             uint64_t da, db;
             if (QUANT) {
@@ -249,24 +256,38 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int mt0 = si.range * p.mt_per_range;
       const int nmt = min(mt0 + p.mt_per_range, p.n_mtiles) - mt0;
-      const __half* e16b = p.e16 + (int64_t)b * p.num_heads * p.l_pad;
       const float* mtb = p.m_tile + (int64_t)b * p.num_heads * p.n_tiles;
       const float* msb = p.m_seq + (int64_t)b * p.num_heads;
+      float lsum[4] = {0.f, 0.f, 0.f, 0.f};   // sum of P of this thread's (head, 4-token) tasks
+      // per-head tile max of the next page, loaded one page ahead (tile = 8 pages)
+      float mseq[4], mt_next[4];
+#pragma unroll
+      for (int tk = 0; tk < 4; ++tk) {
+        const int h = min((wt + 128 * tk) >> 2, p.num_heads - 1);
+        mseq[tk] = msb[h];
+        mt_next[tk] = mtb[(int64_t)h * p.n_tiles + ((si.page0 * 16) >> 7)];
+      }
       for (int pg = 0; pg < si.npages; ++pg, ++it) {
         const int s = it % S;
         if (!mbar_wait(&ctl->pempty[s], ((it / S) & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
-        if (QUANT && !mbar_wait(&ctl->vfull[s], (it / S) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(&ctl->vfull[s], (it / S) & 1, abort_flag, p.status)) { ok = false; break; }
         uint8_t* st = smem + s * LY.stage_bytes;
-        uint8_t* pb = st + LY.v_bytes + LY.a_bytes;
+        uint8_t* pb = st + LY.v_bytes + LY.a_bytes + LY.e_bytes;
+        const uint8_t* es = st + LY.v_bytes + LY.a_bytes;   // e16 [heads][16 tokens]
         const int t0 = (si.page0 + pg) * 16;
-        const int tile = t0 >> 7;
+        const int next_tile = ((si.page0 + min(pg + 1, si.npages - 1)) * 16) >> 7;
         // P rows: thread -> (head, 4 consecutive tokens)
-        for (int task = wt; task < p.nh * 4; task += 128) {
+#pragma unroll
+        for (int tk = 0; tk < 4; ++tk) {
+          const int task = wt + 128 * tk;
+          if (task >= p.nh * 4) break;
           const int h = task >> 2, kq = task & 3;
+          const float mt = mt_next[tk];
+          mt_next[tk] = mtb[(int64_t)min(h, p.num_heads - 1) * p.n_tiles + next_tile];
           float pv4[4] = {0.f, 0.f, 0.f, 0.f};
           if (h < p.num_heads) {
-            const float f = __expf(mtb[(int64_t)h * p.n_tiles + tile] - msb[h]);
-            const uint2 raw = *reinterpret_cast<const uint2*>(e16b + (int64_t)h * p.l_pad + t0 + 4 * kq);
+            const float f = __expf(mt - mseq[tk]);
+            const uint2 raw = *reinterpret_cast<const uint2*>(es + h * 32 + 8 * kq);
             const __half2 e01 = *reinterpret_cast<const __half2*>(&raw.x);
             const __half2 e23 = *reinterpret_cast<const __half2*>(&raw.y);
             const float2 a = __half22float2(e01), c = __half22float2(e23);
@@ -274,6 +295,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               if (t0 + 4 * kq + i >= L) pv4[i] = 0.f;
+            lsum[tk] += (pv4[0] + pv4[1]) + (pv4[2] + pv4[3]);
           }
           if (QUANT) {
 #pragma unroll
@@ -301,35 +323,69 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
           }
         }
         if (QUANT) {
-          // dequantize this page's V nibbles into MN-major f16 A tiles
+          // Dequantize this page's V nibbles into MN-major f16 A tiles. Task = (M-tile,
+          // token, 16-byte window = 32 channels). A window starts at a block-constant
+          // misalignment inside the staged row, so it is cut from two aligned 16-byte
+          // chunks with funnel shifts; 8 nibbles -> 4 half2 with the 0x6400 bias trick.
           uint8_t* ab = st + LY.v_bytes;
-          for (int task = wt; task < nmt * 256; task += 128) {
-            const int m = task >> 8, tt = task & 255;
-            const int k = ((tt >> 7) << 3) | (tt & 7);
-            const int g = (tt >> 3) & 15;
+          const int nvq = p.v_boxes * 8 - 1;    // last staged 16-byte chunk index
+          for (int task = wt; task < nmt * 64; task += 128) {
+            const int m = task >> 6, tt = task & 63;
+            const int k = tt & 15, j = tt >> 4;
             const int gm = mt0 + m;
             const bool outl = gm < p.t_out;
             const int jt = outl ? gm : gm - p.t_out;
-            const int ch_first = (outl ? 0 : p.v_nout) + 128 * jt + 8 * g;
+            const int bb = (outl ? p.vq_off : p.vq_off + p.v_nbo) - p.vx0;   // block start in the staged row
+            const int win = bb + 64 * jt + 16 * j;
+            const int c0 = min(win >> 4, nvq), c1 = min((win >> 4) + 1, nvq);
+            const uint8_t* rowp = st + k * 128;
+            const uint4 A0 = *reinterpret_cast<const uint4*>(rowp + (c0 >> 3) * 2048 + (((c0 & 7) ^ (k & 7)) << 4));
+            const uint4 A1 = *reinterpret_cast<const uint4*>(rowp + (c1 >> 3) * 2048 + (((c1 & 7) ^ (k & 7)) << 4));
+            const uint32_t W8[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
+            const int sh = (bb & 3) * 8;
+            uint32_t w[4];
+            switch ((bb >> 2) & 3) {
+              case 0:
+#pragma unroll
+                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i], W8[i + 1], sh);
+                break;
+              case 1:
+#pragma unroll
+                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i + 1], W8[i + 2], sh);
+                break;
+              case 2:
+#pragma unroll
+                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i + 2], W8[i + 3], sh);
+                break;
+              default:
+#pragma unroll
+                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i + 3], W8[i + 4], sh);
+                break;
+            }
+            const int ch_first = (outl ? 0 : p.v_nout) + 128 * jt + 32 * j;   // channel of nibble 0
             const int ch_end = outl ? p.v_nout : p.v_rank;
-            const int byte0 = (outl ? p.vq_off : p.vq_off + p.v_nbo) + 64 * jt + 4 * g - p.vx0;
-            uint32_t packed[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const int o = byte0 + i;
-              const int c0 = ch_first + 2 * i;
-              uint32_t byte = 0x88u;
-              if (c0 < ch_end) {   // bytes past the block are never read
-                const uint8_t* bx = st + (o >> 7) * 2048 + k * 128;
-                const int w = o & 127;
-                byte = bx[(((w >> 4) ^ (k & 7)) << 4) | (w & 15)];
+              // half2 pairs (e0,e4) (e1,e5) (e2,e6) (e3,e7) of this word's 8 channels
+              uint32_t hv[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t bits = ((w[i] >> (4 * e)) & 0x000F000Fu) | 0x64006400u;   // 1024 + n
+                const __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&bits), __float2half2_rn(1032.f));
+                hv[e] = *reinterpret_cast<const uint32_t*>(&hb);
               }
-              const float lo = (c0 < ch_end) ? (float)((int)(byte & 15u) - 8) : 0.f;
-              const float hi = (c0 + 1 < ch_end) ? (float)((int)(byte >> 4) - 8) : 0.f;
-              const __half2 hv = __floats2half2_rn(lo, hi);
-              packed[i] = *reinterpret_cast<const uint32_t*>(&hv);
+              const int cg0 = ch_first + 8 * i;
+              if (cg0 + 8 > ch_end) {   // block tail: zero channels past the block
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  if (cg0 + e >= ch_end) hv[e] &= 0xFFFF0000u;
+                  if (cg0 + e + 4 >= ch_end) hv[e] &= 0x0000FFFFu;
+                }
+              }
+              const int cg = 4 * j + i;   // channel group within the M-tile
+              *reinterpret_cast<uint4*>(ab + m * 4096 + (k >> 3) * 2048 + cg * 128 + (k & 7) * 16) =
+                  make_uint4(hv[0], hv[1], hv[2], hv[3]);
             }
-            *reinterpret_cast<uint4*>(ab + m * 4096 + tt * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
           }
         }
         fence_proxy_async_smem();
@@ -340,17 +396,31 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
         }
       }
       if (!ok) break;
+      // softmax denominator: the 4 threads of a head sit in adjacent lanes
+      if (si.range == 0) {
+#pragma unroll
+        for (int tk = 0; tk < 4; ++tk) {
+          float v = lsum[tk];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          const int task = wt + 128 * tk;
+          const int h = task >> 2;
+          if ((task & 3) == 0 && task < p.nh * 4 && h < p.num_heads) atomicAdd(p.l_seq + (int64_t)b * p.num_heads + h, v);
+        }
+      }
       // ---- flush the accumulator of this sub-item ----
       if (!mbar_wait(&ctl->accfull, acc_cnt & 1, abort_flag, p.status)) break;
       tc_fence_after();
       const int row = q * 32 + lane;
-      float* pvb = p.pv + (int64_t)b * p.num_heads * p.v_rank;
+      float* pvb = p.pv + (int64_t)b * p.num_heads * p.pv_stride;
       for (int m = 0; m < nmt; ++m) {
         const int gm = mt0 + m;
         int ch, ch_end;
         if (QUANT) {
+          // A rows hold each 8-channel group in the order e0 e4 e1 e5 e2 e6 e3 e7
           const bool outl = gm < p.t_out;
-          ch = (outl ? 128 * gm : p.v_nout + 128 * (gm - p.t_out)) + row;
+          const int r7 = row & 7;
+          ch = (outl ? 128 * gm : p.v_nout + 128 * (gm - p.t_out)) + (row & ~7) + ((r7 >> 1) | ((r7 & 1) << 2));
           ch_end = outl ? p.v_nout : p.v_rank;
         } else {
           ch = gm * 128 + row;
@@ -363,7 +433,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int h = c0 + i;
-              if (h < p.num_heads) atomicAdd(pvb + (int64_t)h * p.v_rank + ch, v[i]);
+              if (h < p.num_heads) atomicAdd(pvb + (int64_t)h * p.pv_stride + ch, v[i]);
             }
           }
         }
@@ -383,7 +453,8 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
   }
 }
 
-int launch_pv(bool quant, const CUtensorMap& tm_v, const PvParams& p, int num_sms, cudaStream_t stream) {
+int launch_pv(bool quant, const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms,
+              cudaStream_t stream) {
   const PvLayout L = pv_layout(quant, p);
   if (L.stages < 2) return STARKV_EINVAL;
   const size_t smem = pv_smem_bytes(quant, p);
@@ -392,9 +463,9 @@ int launch_pv(bool quant, const CUtensorMap& tm_v, const PvParams& p, int num_sm
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return STARKV_ECUDA;
   if (quant)
-    pv_kernel<true><<<num_sms, 192, smem, stream>>>(tm_v, p);
+    pv_kernel<true><<<num_sms, 192, smem, stream>>>(tm_v, tm_e, p);
   else
-    pv_kernel<false><<<num_sms, 192, smem, stream>>>(tm_v, p);
+    pv_kernel<false><<<num_sms, 192, smem, stream>>>(tm_v, tm_e, p);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 

@@ -8,19 +8,22 @@
 // [W, 128] per sequence),
 //     logit[t, h] = sum_{r in head h} x[t, r] * z[t, r],   z = CS[t, :] . AB[r, :]
 // where CS[t] = [cos_t | sin_t] is row t of the rotary table. z is a dense
-// [128 tokens x 128 lanes] x K=128 contraction per chunk: it runs on the
-// tcgen05 tensor core (M=128 tokens, N=128 lanes, K=128, f16 in, f32 in TMEM).
-// The codes x are only used elementwise in the epilogue, so the 4-bit cache is
-// dequantized in registers ((n - 8) * bf16 scale, bit-exact) and never has to
-// be laid out as an MMA operand.
+// [128 tokens x 128 lanes] x K=128 contraction per chunk of lanes: it runs on
+// the tcgen05 tensor core (M=128 tokens, N=128 lanes, K=128, f16 in, f32 out in
+// TMEM). The codes x are only used elementwise in the epilogue, so the 4-bit
+// cache is dequantized in registers ((n - 8) * bf16 scale, bit-exact) and never
+// has to be laid out as an MMA operand.
 //
 // Per tile (one sequence, 128 tokens) the epilogue reduces each head's logits
 // to (tile max m, tile sum l = sum exp(logit - m)) and stores exp(logit - m) as
 // f16 ("e16"); the P.V kernel rescales by exp(m - M) with M the sequence max.
 //
-// Warp roles (persistent CTAs, one per SM): warp 0 TMA producer, warp 1 MMA
-// issuer (also owns the TMEM allocation), warps 2-5 epilogue (one token row per
-// thread, TMEM lanes 0-127).
+// Persistent CTAs (one per SM), warp roles:
+//   warp 0      TMA producer: rotary rows, AB chunks (2-slot ring, from L2),
+//               code pages (3-4 slot ring, from HBM) gathered through the block table;
+//   warp 1      MMA issuer, owns the TMEM allocation (4 z buffers x 128 columns);
+//   warps 2-9   epilogue: thread = token row (TMEM lane) x half of the chunk's
+//               columns; per-head partial sums are merged with shared-memory atomics.
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
 
@@ -30,34 +33,35 @@ namespace {
 
 constexpr int kTile = 128;       // tokens per tile (MMA M)
 constexpr int kChunk = 128;      // lanes per chunk (MMA N)
-constexpr int kTmemBufs = 2;
+constexpr int kTmemBufs = 4;
+constexpr int kAbSlots = 2;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kCsBytes = kTile * 128 * 2;       // f16 [128 tokens][128]
 constexpr int kAbBytes = kChunk * 128 * 2;      // f16 [128 lanes][128]
-constexpr int kMaxStages = 3;
+constexpr int kMaxCodeSlots = 4;
 
 template <bool QUANT>
 struct Layout {
   // bf16 codes: 2 boxes of 64 lanes (128 B) per page; 3.2-bit codes: one box of
   // 64 bytes (128 lanes) per page.
-  static constexpr int kStages = QUANT ? 3 : 2;
+  static constexpr int kCodeSlots = QUANT ? 4 : 3;
   static constexpr int kCodeBoxes = QUANT ? 1 : 2;
   static constexpr int kCodeBoxBytes = QUANT ? 16 * 64 : 16 * 128;
-  static constexpr int kCodeBytes = 8 * kCodeBoxes * kCodeBoxBytes;   // per stage (8 pages)
-  static constexpr int kStageBytes = kAbBytes + kCodeBytes;
+  static constexpr int kCodeBytes = 8 * kCodeBoxes * kCodeBoxBytes;   // per slot (8 pages)
   static constexpr int kOffCs = 0;
-  static constexpr int kOffStages = kOffCs + kCsBytes;
-  static constexpr int kOffScales = kOffStages + kStages * kStageBytes;   // 3.2-bit scale boxes
-  // logits and tables follow the scale boxes (8 pages x ks_boxes x 2 KB)
+  static constexpr int kOffAb = kOffCs + kCsBytes;
+  static constexpr int kOffCodes = kOffAb + kAbSlots * kAbBytes;
+  static constexpr int kOffScales = kOffCodes + kCodeSlots * kCodeBytes;   // 3.2-bit scale boxes
   static __host__ __device__ int off_logits(int ks_boxes) { return kOffScales + ks_boxes * 8 * 2048; }
 };
 
 struct SharedCtl {
-  uint64_t full[kMaxStages];
-  uint64_t empty[kMaxStages];
-  uint64_t epi;            // bounded barrier among the 4 epilogue warps
+  uint64_t ab_full[kAbSlots], ab_empty[kAbSlots];
+  uint64_t code_full[kMaxCodeSlots], code_empty[kMaxCodeSlots];
   uint64_t cs_full, cs_empty, sc_full, sc_empty;
-  uint64_t tfull[kTmemBufs];
-  uint64_t tempty[kTmemBufs];
+  uint64_t tfull[kTmemBufs], tempty[kTmemBufs];
+  uint64_t epi;            // bounded barrier among the epilogue warps
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -71,22 +75,28 @@ __device__ __forceinline__ int find_seq(const int* prefix, int n, int item) {
   return lo;
 }
 
+// n - 8 as float for byte k (0..3) of a word already masked to one nibble per
+// byte: the bytes 0x4B0000nn are the float 2^23 + n.
+__device__ __forceinline__ float nib_f(uint32_t masked, int k) {
+  return __uint_as_float(__byte_perm(masked, 0x4B000000u, 0x7650u | (uint32_t)k)) - 8388616.f;
+}
+
 }  // namespace
 
 size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int ks_boxes) {
   const int nt = k_width / 16;
   size_t bytes = quant ? Layout<true>::off_logits(ks_boxes) : Layout<false>::off_logits(0);
-  bytes += (size_t)num_kv_heads * (kTile + 1) * 4;    // logits [H][129]
-  bytes += (size_t)2 * 4 * num_kv_heads * 4;          // cross-warp max / sum
-  bytes += (size_t)nt * 4;                            // lane-tile table
-  bytes += (size_t)(n + 1) * 4;                       // tile prefix over sequences
+  bytes += (size_t)num_kv_heads * (kTile + 1) * 4;            // logits [H][129]
+  bytes += (size_t)2 * kEpiWarps * num_kv_heads * 4;          // cross-warp max / sum
+  bytes += (size_t)nt * 4;                                    // lane-tile table
+  bytes += (size_t)(n + 1) * 4;                               // tile prefix over sequences
   bytes = (bytes + 15) & ~size_t(15);
-  bytes += sizeof(SharedCtl) + 1024;                  // control + alignment slack
+  bytes += sizeof(SharedCtl) + 1024;                          // control + alignment slack
   return bytes;
 }
 
-template <bool QUANT>
-__global__ void __launch_bounds__(192, 1)
+template <bool QUANT, bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
 scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__ CUtensorMap tm_ab,
               const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
               const ScoresParams p) {
@@ -98,59 +108,63 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
   const int NC = (p.k_width + kChunk - 1) / kChunk;
   const int ks_boxes = QUANT ? p.ks_boxes : 0;
   float* logits = reinterpret_cast<float*>(smem + LY::off_logits(ks_boxes));   // [H][129]
-  float* red_m = logits + H * (kTile + 1);                            // [4][H]
-  float* red_l = red_m + 4 * H;                                       // [4][H]
-  int* tiles = reinterpret_cast<int*>(red_l + 4 * H);                 // [NT]
-  int* prefix = tiles + NT;                                           // [n+1]
-  SharedCtl* ctl = reinterpret_cast<SharedCtl*>((reinterpret_cast<uintptr_t>(prefix + p.n + 1) + 15) & ~uintptr_t(15));
+  float* red_m = logits + H * (kTile + 1);                                      // [8][H]
+  float* red_l = red_m + kEpiWarps * H;                                         // [8][H]
+  int* tiles = reinterpret_cast<int*>(red_l + kEpiWarps * H);                   // [NT]
+  int* prefix = tiles + NT;                                                     // [n+1]
+  SharedCtl* ctl =
+      reinterpret_cast<SharedCtl*>((reinterpret_cast<uintptr_t>(prefix + p.n + 1) + 15) & ~uintptr_t(15));
   volatile int* abort_flag = &ctl->abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- prologue: tables, barriers, TMEM ----
+  // ---- prologue: tables, zeroed logits, barriers, TMEM ----
   if (threadIdx.x == 0) {
     int acc = 0;
     for (int b = 0; b < p.n; ++b) {
       prefix[b] = acc;
-      int L = p.seq_lens[b];
-      L = L < 0 ? 0 : (L > p.max_seq_len ? p.max_seq_len : L);
+      const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       acc += (L + kTile - 1) / kTile * p.group;
     }
     prefix[p.n] = acc;
   }
   for (int t = threadIdx.x; t < NT; t += blockDim.x) {
-    int entry = -1;
+    int entry = -1;   // head | outlier lanes << 16 (3.2-bit)
     if (QUANT) {
-      int h = p.tile_head[t];
-      if (h >= 0 && h < H) entry = h | (min(max(p.tile_nout[t], 0), 16) << 16) | ((p.tile_last[t] != 0) << 24);
+      const int h = p.tile_head[t];
+      if (h >= 0 && h < H) entry = h | (min(max(p.tile_nout[t], 0), 16) << 16);
       else record_status(p.status, STARKV_EBOUNDS);
     } else {
       for (int h = 0; h < H; ++h) {
-        int off = p.k_head_offsets[h], r = p.k_ranks[h];
-        int w = (r + 15) & ~15;
+        const int off = p.k_head_offsets[h], w = (p.k_ranks[h] + 15) & ~15;
         if (16 * t >= off && 16 * t < off + w) {
-          entry = h | ((16 * t + 16 >= off + w) << 24);
+          entry = h;
           break;
         }
       }
     }
     tiles[t] = entry;
   }
+  for (int i = threadIdx.x; i < H * (kTile + 1); i += blockDim.x) logits[i] = 0.f;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < LY::kStages; ++s) {
-      mbar_init(&ctl->full[s], 1);
-      mbar_init(&ctl->empty[s], 1 + 4);
+    for (int s = 0; s < kAbSlots; ++s) {
+      mbar_init(&ctl->ab_full[s], 1);
+      mbar_init(&ctl->ab_empty[s], 1);
     }
-    mbar_init(&ctl->epi, 128);
+    for (int s = 0; s < LY::kCodeSlots; ++s) {
+      mbar_init(&ctl->code_full[s], 1);
+      mbar_init(&ctl->code_empty[s], kEpiWarps);
+    }
     mbar_init(&ctl->cs_full, 1);
     mbar_init(&ctl->cs_empty, 1);
     mbar_init(&ctl->sc_full, 1);
-    mbar_init(&ctl->sc_empty, 4);
+    mbar_init(&ctl->sc_empty, kEpiWarps);
     for (int i = 0; i < kTmemBufs; ++i) {
       mbar_init(&ctl->tfull[i], 1);
-      mbar_init(&ctl->tempty[i], 4);
+      mbar_init(&ctl->tempty[i], kEpiWarps);
     }
+    mbar_init(&ctl->epi, 32 * kEpiWarps);
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -168,15 +182,16 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       tma_prefetch(&tm_ab);
       tma_prefetch(&tm_codes);
       if (QUANT) tma_prefetch(&tm_scales);
-      uint32_t it = 0, item_cnt = 0;
+      uint32_t ab_it = 0, code_it = 0, item_cnt = 0;
       for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x, ++item_cnt) {
         const int b = find_seq(prefix, p.n, item);
         const int rem = item - prefix[b];
         const int j = rem % p.group;
         const int tile = rem / p.group;
-        int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
+        const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
         const int t0 = tile * kTile;
         int blk[8], slot[8];
+#pragma unroll
         for (int pg = 0; pg < 8; ++pg) {
           const int t = t0 + 16 * pg;
           blk[pg] = 0;
@@ -207,18 +222,24 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
                           p.ks_x0 + 128 * jb, slot[pg], blk[pg]);
         }
         const int ab_row0 = (b * p.group + j) * p.k_width;
-        for (int c = 0; c < NC; ++c, ++it) {
-          const int s = it % LY::kStages;
-          if (!mbar_wait(&ctl->empty[s], ((it / LY::kStages) & 1) ^ 1, abort_flag, p.status)) break;
-          uint8_t* st = smem + LY::kOffStages + s * LY::kStageBytes;
-          mbar_arrive_expect_tx(&ctl->full[s], LY::kStageBytes);
-          tma_load_2d(st, &tm_ab, &ctl->full[s], 0, ab_row0 + c * kChunk);
-          tma_load_2d(st + kAbBytes / 2, &tm_ab, &ctl->full[s], 64, ab_row0 + c * kChunk);
+        for (int c = 0; c < NC; ++c, ++ab_it, ++code_it) {
+          const int sa = ab_it % kAbSlots;
+          if (!mbar_wait(&ctl->ab_empty[sa], ((ab_it / kAbSlots) & 1) ^ 1, abort_flag, p.status)) break;
+          uint8_t* abs = smem + LY::kOffAb + sa * kAbBytes;
+          mbar_arrive_expect_tx(&ctl->ab_full[sa], kAbBytes);
+          tma_load_2d(abs, &tm_ab, &ctl->ab_full[sa], 0, ab_row0 + c * kChunk);
+          tma_load_2d(abs + kAbBytes / 2, &tm_ab, &ctl->ab_full[sa], 64, ab_row0 + c * kChunk);
+          const int sc = code_it % LY::kCodeSlots;
+          if (!mbar_wait(&ctl->code_empty[sc], ((code_it / LY::kCodeSlots) & 1) ^ 1, abort_flag, p.status)) break;
+          uint8_t* cds = smem + LY::kOffCodes + sc * LY::kCodeBytes;
+          mbar_arrive_expect_tx(&ctl->code_full[sc], LY::kCodeBytes);
+#pragma unroll
           for (int pg = 0; pg < 8; ++pg)
+#pragma unroll
             for (int i = 0; i < LY::kCodeBoxes; ++i) {
               const int x = QUANT ? c * 64 : c * kChunk + 64 * i;
-              tma_load_3d(st + kAbBytes + (i * 8 + pg) * LY::kCodeBoxBytes, &tm_codes, &ctl->full[s], x,
-                          slot[pg], blk[pg]);
+              tma_load_3d(cds + (i * 8 + pg) * LY::kCodeBoxBytes, &tm_codes, &ctl->code_full[sc], x, slot[pg],
+                          blk[pg]);
             }
         }
       }
@@ -227,40 +248,42 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     // ================= MMA issuer =================
     if (lane == 0) {
       const uint32_t idesc = instr_desc_f16(/*f16*/ 0, 0, 0, kTile, kChunk);
-      uint32_t it = 0, tb = 0, item_cnt = 0;
+      uint32_t ab_it = 0, tb = 0, item_cnt = 0;
       const uint32_t cs_addr = smem_u32(smem + LY::kOffCs);
       for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x, ++item_cnt) {
         if (!mbar_wait(&ctl->cs_full, item_cnt & 1, abort_flag, p.status)) break;
         tc_fence_after();
-        for (int c = 0; c < NC; ++c, ++it, ++tb) {
-          const int s = it % LY::kStages;
+        for (int c = 0; c < NC; ++c, ++ab_it, ++tb) {
+          const int sa = ab_it % kAbSlots;
           const int buf = tb % kTmemBufs;
-          if (!mbar_wait(&ctl->full[s], (it / LY::kStages) & 1, abort_flag, p.status)) break;
+          if (!mbar_wait(&ctl->ab_full[sa], (ab_it / kAbSlots) & 1, abort_flag, p.status)) break;
           if (!mbar_wait(&ctl->tempty[buf], ((tb / kTmemBufs) & 1) ^ 1, abort_flag, p.status)) break;
           tc_fence_after();
-          const uint32_t ab_addr = smem_u32(smem + LY::kOffStages + s * LY::kStageBytes);
+          const uint32_t ab_addr = smem_u32(smem + LY::kOffAb + sa * kAbBytes);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t koff = (kk >> 2) * (kCsBytes / 2) + (kk & 3) * 32;
-            const uint64_t da = smem_desc(cs_addr + koff, 16, 1024, kSwizzle128B);
+            const uint64_t da = smem_desc(cs_addr + (kk >> 2) * (kCsBytes / 2) + (kk & 3) * 32, 16, 1024,
+                                          kSwizzle128B);
             const uint64_t db = smem_desc(ab_addr + (kk >> 2) * (kAbBytes / 2) + (kk & 3) * 32, 16, 1024,
                                           kSwizzle128B);
             umma_f16(tmem + buf * kChunk, da, db, idesc, kk > 0);
           }
-          umma_commit(&ctl->empty[s]);
+          umma_commit(&ctl->ab_empty[sa]);
           umma_commit(&ctl->tfull[buf]);
         }
         umma_commit(&ctl->cs_empty);
       }
     }
   } else {
-    // ================= epilogue (warps 2..5) =================
+    // ================= epilogue (warps 2..9) =================
+    const int ew = warp - 2;              // 0..7
     const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = ew >> 2;             // which 64 columns of each chunk
     const int row = q * 32 + lane;        // token within the tile
-    const int e = warp - 2;               // 0..3, for the cross-warp reductions
-    uint32_t it = 0, tb = 0, item_cnt = 0, epi_phase = 0;
-    // Bounded barrier among the 128 epilogue threads (a plain bar.sync could
-    // wait forever if another epilogue warp left on a timed-out pipeline wait).
+    const int pg = row >> 4, sl = row & 15;
+    uint32_t code_it = 0, tb = 0, item_cnt = 0, epi_phase = 0;
+    // Bounded barrier among the epilogue threads (a plain bar.sync could wait
+    // forever if another epilogue warp left on a timed-out pipeline wait).
     auto epi_sync = [&]() -> bool {
       mbar_arrive(&ctl->epi);
       return mbar_wait(&ctl->epi, (epi_phase++) & 1, abort_flag, p.status);
@@ -273,129 +296,170 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       const int tile = rem / p.group;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int t0 = tile * kTile;
-      const int pg = row >> 4, sl = row & 15;
       if (QUANT && !mbar_wait(&ctl->sc_full, item_cnt & 1, abort_flag, p.status)) break;
-      float acc = 0.f;
+      // running sums of the current head: 4 independent chains (bf16: all lanes;
+      // 3.2-bit: outlier / inlier lanes, scaled at the flush)
+      float ao[4] = {0.f, 0.f, 0.f, 0.f}, ai[4] = {0.f, 0.f, 0.f, 0.f};
+      int cur_h = -1;
+      auto flush = [&]() {
+        float v;
+        if (QUANT) {
+          // (outlier, inlier) bf16 scales of head cur_h for this token
+          const int off = p.ks_off + 4 * cur_h - p.ks_x0;
+          const int jb = off >> 7, within = off & 127;
+          const uint8_t* sb = smem + LY::kOffScales + (jb * 8 + pg) * 2048 + sl * 128;
+          const uint32_t sw =
+              *reinterpret_cast<const uint32_t*>(sb + ((((within >> 4) ^ (sl & 7)) << 4) | (within & 15)));
+          const float so = __uint_as_float(sw << 16), si = __uint_as_float(sw & 0xFFFF0000u);
+          v = so * ((ao[0] + ao[1]) + (ao[2] + ao[3])) + si * ((ai[0] + ai[1]) + (ai[2] + ai[3]));
+        } else {
+          v = (ai[0] + ai[1]) + (ai[2] + ai[3]);
+        }
+        atomicAdd(&logits[cur_h * (kTile + 1) + row], v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ao[i] = ai[i] = 0.f;
+      };
       bool ok = true;
-      for (int c = 0; c < NC; ++c, ++it, ++tb) {
-        const int s = it % LY::kStages;
+      for (int c = 0; c < NC; ++c, ++code_it, ++tb) {
+        const int sc = code_it % LY::kCodeSlots;
         const int buf = tb % kTmemBufs;
         if (!mbar_wait(&ctl->tfull[buf], (tb / kTmemBufs) & 1, abort_flag, p.status) ||
-            !mbar_wait(&ctl->full[s], (it / LY::kStages) & 1, abort_flag, p.status)) {
+            !mbar_wait(&ctl->code_full[sc], (code_it / LY::kCodeSlots) & 1, abort_flag, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint8_t* codes = smem + LY::kOffStages + s * LY::kStageBytes + kAbBytes;
-#pragma unroll 1
-        for (int g = 0; g < kChunk / 32; ++g) {
-          const int tau0 = (c * kChunk + 32 * g) >> 4;
-          if (tau0 >= NT) break;
-          float z[32];
-          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk + 32 * g, z);
+        const uint8_t* codes = smem + LY::kOffCodes + sc * LY::kCodeBytes;
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk;
+        // this warp's 32-lane groups of the chunk: 2*half and 2*half+1
+        const int ng = min(2, max(0, (NT * 16 - c * kChunk - 64 * half + 31) / 32));
+        uint32_t zr[2][32];
+        if (ng > 0) {
+          tmem_ld32_issue(trow + 64 * half, zr[0]);
+          tmem_wait(zr[0]);
+        }
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+          if (gi >= ng) break;
+          const int g = 2 * half + gi;
+          if (gi + 1 < ng) tmem_ld32_issue(trow + 32 * (g + 1), zr[1]);
+          const uint32_t* z = zr[gi];
           float x[32];
           if (QUANT) {
-            // 16 bytes = 32 nibbles of this token's lanes [32g, 32g+32) of the chunk
+            // 16 bytes = 32 nibbles: this token's lanes [32g, 32g+32) of the chunk
             const uint8_t* box = codes + pg * LY::kCodeBoxBytes;
             const int phys = g ^ ((sl >> 1) & 3);     // 64-byte swizzle
-            uint4 u = *reinterpret_cast<const uint4*>(box + sl * 64 + phys * 16);
+            const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 64 + phys * 16);
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int i = 0; i < 32; ++i) x[i] = (float)(int)((w[i >> 3] >> (4 * (i & 7))) & 15u) - 8.f;
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t lo = w[k] & 0x0F0F0F0Fu, hi = (w[k] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+              for (int bb = 0; bb < 4; ++bb) {
+                x[8 * k + 2 * bb] = nib_f(lo, bb);
+                x[8 * k + 2 * bb + 1] = nib_f(hi, bb);
+              }
+            }
           } else {
             const uint8_t* box = codes + ((g >> 1) * 8 + pg) * LY::kCodeBoxBytes;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
-              const int chunk16 = (g & 1) * 4 + v;
-              const int phys = chunk16 ^ (sl & 7);      // 128-byte swizzle
-              uint4 u = *reinterpret_cast<const uint4*>(box + sl * 128 + phys * 16);
+              const int phys = ((g & 1) * 4 + v) ^ (sl & 7);   // 128-byte swizzle
+              const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 128 + phys * 16);
               float f[8];
-              if (p.cache_dtype == STARKV_BF16) bf16x8_to_f32(u, f); else f16x8_to_f32(u, f);
+              if (F16) f16x8_to_f32(u, f); else bf16x8_to_f32(u, f);
 #pragma unroll
               for (int i = 0; i < 8; ++i) x[8 * v + i] = f[i];
             }
           }
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int tau = tau0 + hh;
+            const int tau = ((c * kChunk + 32 * g) >> 4) + hh;
             if (tau >= NT) break;
             const int meta = tiles[tau];
             if (meta < 0) continue;
             const int h = meta & 0xFFFF;
-            float part = 0.f;
-            if (QUANT) {
-              // (outlier, inlier) bf16 scales of head h for this token
-              const int off = p.ks_off + 4 * h - p.ks_x0;
-              const int jb = off >> 7, within = off & 127;
-              const uint8_t* sb = smem + LY::kOffScales + (jb * 8 + pg) * 2048 + sl * 128;
-              const uint32_t sw = *reinterpret_cast<const uint32_t*>(
-                  sb + ((((within >> 4) ^ (sl & 7)) << 4) | (within & 15)));
-              const float so = __uint_as_float(sw << 16), si = __uint_as_float(sw & 0xFFFF0000u);
-              const int nout = (meta >> 16) & 0xFF;
+            if (h != cur_h) {
+              if (cur_h >= 0) flush();
+              cur_h = h;
+            }
+            const int nout = QUANT ? (meta >> 16) & 0xFF : 0;
+            if (nout == 0) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) part += x[16 * hh + i] * (i < nout ? so : si) * z[16 * hh + i];
+              for (int i = 0; i < 16; ++i) ai[i & 3] = fmaf(x[16 * hh + i], __uint_as_float(z[16 * hh + i]), ai[i & 3]);
+            } else if (nout == 16) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) ao[i & 3] = fmaf(x[16 * hh + i], __uint_as_float(z[16 * hh + i]), ao[i & 3]);
             } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) part += x[16 * hh + i] * z[16 * hh + i];
-            }
-            acc += part;
-            if (meta & (1 << 24)) {
-              logits[h * (kTile + 1) + row] = acc;
-              acc = 0.f;
+              for (int i = 0; i < 16; ++i) {
+                const float t = x[16 * hh + i] * __uint_as_float(z[16 * hh + i]);
+                if (i < nout) ao[i & 3] += t; else ai[i & 3] += t;
+              }
             }
           }
+          if (gi + 1 < ng) tmem_wait(zr[1]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&ctl->tempty[buf]);
-          mbar_arrive(&ctl->empty[s]);
+          mbar_arrive(&ctl->code_empty[sc]);
         }
       }
+      if (cur_h >= 0) flush();
       if (QUANT) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->sc_empty);
       }
       if (!ok || !epi_sync()) break;
-      // ---- per-head tile softmax statistics ----
+      // ---- per-head tile softmax statistics: warp ew owns tokens [16 ew, 16 ew + 16) ----
       for (int h = lane; h < H; h += 32) {
         float m = -INFINITY;
-        for (int i = 0; i < 32; ++i) {
-          const int t = 32 * e + i;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int t = 16 * ew + i;
           if (t0 + t < L) m = fmaxf(m, logits[h * (kTile + 1) + t]);
         }
-        red_m[e * H + h] = m;
+        red_m[ew * H + h] = m;
       }
       if (!epi_sync()) break;
       for (int h = lane; h < H; h += 32) {
-        const float m = fmaxf(fmaxf(red_m[h], red_m[H + h]), fmaxf(red_m[2 * H + h], red_m[3 * H + h]));
+        float m = red_m[h];
+        for (int w2 = 1; w2 < kEpiWarps; ++w2) m = fmaxf(m, red_m[w2 * H + h]);
         const int hq = h * p.group + j;
         float ssum = 0.f;
-        __align__(16) __half ev[32];
-        for (int i = 0; i < 32; ++i) {
-          const int t = 32 * e + i;
+        __align__(16) __half ev[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int t = 16 * ew + i;
           float v = 0.f;
           if (t0 + t < L) v = __expf(logits[h * (kTile + 1) + t] - m);
           ssum += v;
           ev[i] = __float2half_rn(v);
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + 32 * e);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) dst[v] = reinterpret_cast<const uint4*>(ev)[v];
-        red_l[e * H + h] = ssum;
+        uint4* dst = reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + 16 * ew);
+        dst[0] = reinterpret_cast<const uint4*>(ev)[0];
+        dst[1] = reinterpret_cast<const uint4*>(ev)[1];
+        red_l[ew * H + h] = ssum;
       }
       if (!epi_sync()) break;
-      if (e == 0) {
+      if (ew == 0) {
         for (int h = lane; h < H; h += 32) {
-          const float m = fmaxf(fmaxf(red_m[h], red_m[H + h]), fmaxf(red_m[2 * H + h], red_m[3 * H + h]));
-          const float l = red_l[h] + red_l[H + h] + red_l[2 * H + h] + red_l[3 * H + h];
+          float m = red_m[h], l = red_l[h];
+          for (int w2 = 1; w2 < kEpiWarps; ++w2) {
+            m = fmaxf(m, red_m[w2 * H + h]);
+            l += red_l[w2 * H + h];
+          }
           const int hq = h * p.group + j;
           const int64_t mi = ((int64_t)b * p.num_heads + hq) * p.n_tiles + tile;
           p.m_tile[mi] = m;
-          p.l_tile[mi] = l;
+          (void)l;
           atomic_max_f32(p.m_seq + (int64_t)b * p.num_heads + hq, m);
         }
       }
+      // clear the logits for the next tile's atomic flushes
+      for (int i = threadIdx.x - 64; i < H * (kTile + 1); i += 32 * kEpiWarps) logits[i] = 0.f;
       if (!epi_sync()) break;
     }
   }
@@ -413,14 +477,18 @@ int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab
                   const CUtensorMap& tm_scales, const ScoresParams& p, int num_sms, cudaStream_t stream) {
   const size_t smem = scores_smem_bytes(quant, p.num_kv_heads, p.n, p.k_width, quant ? p.ks_boxes : 0);
   if (smem > 227 * 1024) return STARKV_EINVAL;
-  const void* fn = quant ? (const void*)scores_kernel<true> : (const void*)scores_kernel<false>;
+  const bool f16 = p.cache_dtype == STARKV_F16;
+  const void* fn = quant ? (const void*)scores_kernel<true, false>
+                         : (f16 ? (const void*)scores_kernel<false, true> : (const void*)scores_kernel<false, false>);
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return STARKV_ECUDA;
   const int grid = num_sms;
   if (quant)
-    scores_kernel<true><<<grid, 192, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
+    scores_kernel<true, false><<<grid, kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
+  else if (f16)
+    scores_kernel<false, true><<<grid, kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
   else
-    scores_kernel<false><<<grid, 192, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
+    scores_kernel<false, false><<<grid, kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 

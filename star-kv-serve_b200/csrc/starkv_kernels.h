@@ -16,9 +16,10 @@ struct Workspace {
   size_t cs;         // f16 [l_pad, 128]                rotary table rows 0..l_pad-1
   size_t e16;        // f16 [n, num_heads, l_pad]       exp(logit - tile max)
   size_t m_tile;     // f32 [n, num_heads, n_tiles]     tile max
-  size_t l_tile;     // f32 [n, num_heads, n_tiles]     tile sum of exp
+  size_t l_seq;      // f32 [n, num_heads]              softmax denominator sum_t p_t
   size_t m_seq;      // f32 [n, num_heads]              sequence max
-  size_t pv;         // f32 [n, num_heads, v_rank]      sum_t p_t * V_t (unnormalised)
+  size_t pv;         // f32 [n, num_heads, pv_stride]   sum_t p_t * V_t (unnormalised), zero padded
+  int pv_stride;     // v_rank rounded up to 64
   size_t total;
   int l_pad, n_tiles;
 };
@@ -40,7 +41,6 @@ struct ScoresParams {
   int ks_off, ks_x0, ks_boxes;     // 3.2-bit: K scales at ks_off; boxes of 128 B from ks_x0
   __half* e16;
   float* m_tile;
-  float* l_tile;
   float* m_seq;
   int l_pad, n_tiles;
   int32_t* status;
@@ -63,20 +63,20 @@ struct PvParams {
   const __half* e16;
   const float* m_tile;
   const float* m_seq;
+  float* l_seq;
   float* pv;
+  int pv_stride;
   int l_pad, n_tiles;
   int32_t* status;
 };
 
 struct LiftParams {
-  const float* pv;        // [n, H, rv]
-  const float* m_tile;
-  const float* l_tile;
-  const float* m_seq;
+  const float* pv;        // [n, H, pv_stride]
+  int pv_stride;
+  const float* l_seq;
   const void* v_up; int64_t vu_s0, vu_s1, vu_s2; int v_up_dtype;   // [H, rv, Hd]
   void* out; int64_t o_s0, o_s1, o_s2; int out_dtype;              // [n, H, Hd]
-  const int32_t* seq_lens;
-  int n, num_heads, v_rank, head_dim, n_tiles, max_seq_len;
+  int n, num_heads, v_rank, head_dim;
 };
 
 struct FoldParams {
@@ -92,7 +92,7 @@ struct FoldParams {
   const void* cs; int64_t cs_s0, cs_s1; int cs_dtype; int cs_rows;
   __half* cs16; int l_pad, max_seq_len;
   // per-call initialisation
-  float* m_seq; int m_count;
+  float* m_seq; float* l_seq; int m_count;
   float* pv; int64_t pv_count;
   int32_t* status;
 };
@@ -103,7 +103,8 @@ size_t pv_smem_bytes(bool quant, const PvParams& p);
 int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream);
 int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_codes,
                   const CUtensorMap& tm_scales, const ScoresParams& p, int num_sms, cudaStream_t stream);
-int launch_pv(bool quant, const CUtensorMap& tm_v, const PvParams& p, int num_sms, cudaStream_t stream);
+int launch_pv(bool quant, const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms,
+              cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
 
 }  // namespace starkv
