@@ -165,42 +165,67 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
 
   if (warp == 0) {
     // ================= TMA producer =================
+    // All 32 lanes fetch block-table entries (32 pages per batch, one batch
+    // ahead, so the table's latency is never on the issue path); lane 0 issues
+    // the copies.
     if (lane == 0) {
       tma_prefetch(&tm_v);
       tma_prefetch(&tm_e);
-      const int e_bytes = p.num_heads * 32;
-      uint32_t it = 0;
-      int u = u_begin;
-      SubItem si;
-      while (!*abort_flag && next_sub(u, u_end, total_pages, pprefix, p.n, si)) {
-        const int mt0 = si.range * p.mt_per_range;
-        const int mt1 = min(mt0 + p.mt_per_range, p.n_mtiles);
-        for (int pg = 0; pg < si.npages; ++pg, ++it) {
+    }
+    const int e_bytes = p.num_heads * 32;
+    auto block_of = [&](int b, int page, int npages_end) -> int {
+      if (page >= npages_end) return 0;
+      const int col = (page * 16) / p.block_size;
+      int blk = -1;
+      if (col < p.max_blocks) blk = p.block_table[(int64_t)b * p.bt_s0 + (int64_t)col * p.bt_s1];
+      if (blk < 0 || blk >= p.num_blocks) {
+        record_status(p.status, STARKV_EBOUNDS);
+        blk = 0;
+      }
+      return blk;
+    };
+    uint32_t it = 0;
+    int u = u_begin;
+    SubItem si;
+    bool stop = false;
+    while (!stop && next_sub(u, u_end, total_pages, pprefix, p.n, si)) {
+      const int mt0 = si.range * p.mt_per_range;
+      const int mt1 = min(mt0 + p.mt_per_range, p.n_mtiles);
+      const int pend = si.page0 + si.npages;
+      int ids_cur = block_of(si.b, si.page0 + lane, pend);
+      int ids_nxt = block_of(si.b, si.page0 + 32 + lane, pend);
+      for (int pg = 0; pg < si.npages; ++pg, ++it) {
+        if (pg > 0 && (pg & 31) == 0) {
+          ids_cur = ids_nxt;
+          ids_nxt = block_of(si.b, si.page0 + pg + 32 + lane, pend);
+        }
+        const int blk = __shfl_sync(0xffffffffu, ids_cur, pg & 31);
+        int ok = 1;
+        if (lane == 0) {
           const int s = it % S;
-          if (!mbar_wait(&ctl->vempty[s], ((it / S) & 1) ^ 1, abort_flag, p.status)) break;
-          const int t = (si.page0 + pg) * 16;
-          const int col = t / p.block_size;
-          int blk = -1;
-          if (col < p.max_blocks) blk = p.block_table[(int64_t)si.b * p.bt_s0 + (int64_t)col * p.bt_s1];
-          if (blk < 0 || blk >= p.num_blocks) {
-            record_status(p.status, STARKV_EBOUNDS);
-            blk = 0;
+          ok = mbar_wait(&ctl->vempty[s], ((it / S) & 1) ^ 1, abort_flag, p.status) ? 1 : 0;
+          if (ok) {
+            const int t = (si.page0 + pg) * 16;
+            const int slot = t % p.block_size;
+            uint8_t* st = smem + s * LY.stage_bytes;
+            if (QUANT) {
+              mbar_arrive_expect_tx(&ctl->vfull[s], p.v_boxes * 2048 + e_bytes);
+              for (int jb = 0; jb < p.v_boxes; ++jb)
+                tma_load_3d(st + jb * 2048, &tm_v, &ctl->vfull[s], p.vx0 + 128 * jb, slot, blk);
+            } else {
+              mbar_arrive_expect_tx(&ctl->vfull[s], (mt1 - mt0) * 4096 + e_bytes);
+              for (int m = mt0; m < mt1; ++m)
+                for (int i = 0; i < 2; ++i)
+                  tma_load_3d(st + (m - mt0) * 4096 + i * 2048, &tm_v, &ctl->vfull[s], p.k_width + m * 128 + 64 * i,
+                              slot, blk);
+            }
+            // e16 rows of this sequence's heads for the page's 16 tokens
+            tma_load_2d(st + LY.v_bytes + LY.a_bytes, &tm_e, &ctl->vfull[s], t, si.b * p.num_heads);
           }
-          const int slot = t % p.block_size;
-          uint8_t* st = smem + s * LY.stage_bytes;
-          if (QUANT) {
-            mbar_arrive_expect_tx(&ctl->vfull[s], p.v_boxes * 2048 + e_bytes);
-            for (int jb = 0; jb < p.v_boxes; ++jb)
-              tma_load_3d(st + jb * 2048, &tm_v, &ctl->vfull[s], p.vx0 + 128 * jb, slot, blk);
-          } else {
-            mbar_arrive_expect_tx(&ctl->vfull[s], (mt1 - mt0) * 4096 + e_bytes);
-            for (int m = mt0; m < mt1; ++m)
-              for (int i = 0; i < 2; ++i)
-                tma_load_3d(st + (m - mt0) * 4096 + i * 2048, &tm_v, &ctl->vfull[s], p.k_width + m * 128 + 64 * i,
-                            slot, blk);
-          }
-          // e16 rows of this sequence's heads for the page's 16 tokens
-          tma_load_2d(st + LY.v_bytes + LY.a_bytes, &tm_e, &ctl->vfull[s], t, si.b * p.num_heads);
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          stop = true;
+          break;
         }
       }
     }

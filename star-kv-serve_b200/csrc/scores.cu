@@ -88,7 +88,7 @@ size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int k
   size_t bytes = quant ? Layout<true>::off_logits(ks_boxes) : Layout<false>::off_logits(0);
   bytes += (size_t)num_kv_heads * (kTile + 1) * 4;            // logits [H][129]
   bytes += (size_t)2 * kEpiWarps * num_kv_heads * 4;          // cross-warp max / sum
-  bytes += (size_t)nt * 4;                                    // lane-tile table
+  bytes += 16 + (size_t)(nt + 7) / 8 * 8 * 4;                // lane-tile table, padded to whole chunks
   bytes += (size_t)(n + 1) * 4;                               // tile prefix over sequences
   bytes = (bytes + 15) & ~size_t(15);
   bytes += sizeof(SharedCtl) + 1024;                          // control + alignment slack
@@ -110,8 +110,9 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
   float* logits = reinterpret_cast<float*>(smem + LY::off_logits(ks_boxes));   // [H][129]
   float* red_m = logits + H * (kTile + 1);                                      // [8][H]
   float* red_l = red_m + kEpiWarps * H;                                         // [8][H]
-  int* tiles = reinterpret_cast<int*>(red_l + kEpiWarps * H);                   // [NT]
-  int* prefix = tiles + NT;                                                     // [n+1]
+  int* tiles = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(red_l + kEpiWarps * H) + 15) &
+                                      ~uintptr_t(15));                          // [NC * 8], -1 past NT
+  int* prefix = tiles + NC * 8;                                                 // [n+1]
   SharedCtl* ctl =
       reinterpret_cast<SharedCtl*>((reinterpret_cast<uintptr_t>(prefix + p.n + 1) + 15) & ~uintptr_t(15));
   volatile int* abort_flag = &ctl->abort_flag;
@@ -129,9 +130,10 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     }
     prefix[p.n] = acc;
   }
-  for (int t = threadIdx.x; t < NT; t += blockDim.x) {
+  for (int t = threadIdx.x; t < NC * 8; t += blockDim.x) {
     int entry = -1;   // head | outlier lanes << 16 (3.2-bit)
-    if (QUANT) {
+    if (t >= NT) {
+    } else if (QUANT) {
       const int h = p.tile_head[t];
       if (h >= 0 && h < H) entry = h | (min(max(p.tile_nout[t], 0), 16) << 16);
       else record_status(p.status, STARKV_EBOUNDS);
@@ -177,60 +179,80 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
 
   if (warp == 0) {
     // ================= TMA producer =================
+    // Lanes 0-7 fetch the 8 block ids of the NEXT tile while lane 0 issues the
+    // current tile's copies, so the block table's latency stays off the issue path.
     if (lane == 0) {
       tma_prefetch(&tm_cs);
       tma_prefetch(&tm_ab);
       tma_prefetch(&tm_codes);
       if (QUANT) tma_prefetch(&tm_scales);
-      uint32_t ab_it = 0, code_it = 0, item_cnt = 0;
-      for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x, ++item_cnt) {
+    }
+    auto block_of = [&](int item) -> int {   // block id of page `lane` of an item (lanes 0-7)
+      if (item >= total_items || lane >= 8) return 0;
+      const int b = find_seq(prefix, p.n, item);
+      const int tile = (item - prefix[b]) / p.group;
+      const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
+      const int t = tile * kTile + 16 * lane;
+      if (t >= L) return 0;
+      const int col = t / p.block_size;
+      int id = -1;
+      if (col < p.max_blocks) id = p.block_table[(int64_t)b * p.bt_s0 + (int64_t)col * p.bt_s1];
+      if (id < 0 || id >= p.num_blocks) {
+        record_status(p.status, STARKV_EBOUNDS);
+        id = 0;
+      }
+      return id;
+    };
+    uint32_t ab_it = 0, code_it = 0, item_cnt = 0;
+    int ids_next = block_of(blockIdx.x);
+    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++item_cnt) {
+      const int ids = ids_next;
+      ids_next = block_of(item + gridDim.x);
+      int blk[8], slot[8];
+#pragma unroll
+      for (int pg = 0; pg < 8; ++pg) blk[pg] = __shfl_sync(0xffffffffu, ids, pg);
+      int ok = 1;
+      if (lane == 0) {
         const int b = find_seq(prefix, p.n, item);
         const int rem = item - prefix[b];
         const int j = rem % p.group;
         const int tile = rem / p.group;
-        const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
         const int t0 = tile * kTile;
-        int blk[8], slot[8];
 #pragma unroll
-        for (int pg = 0; pg < 8; ++pg) {
-          const int t = t0 + 16 * pg;
-          blk[pg] = 0;
-          slot[pg] = 0;
-          if (t < L) {
-            const int col = t / p.block_size;
-            int id = -1;
-            if (col < p.max_blocks) id = p.block_table[(int64_t)b * p.bt_s0 + (int64_t)col * p.bt_s1];
-            if (id < 0 || id >= p.num_blocks) {
-              record_status(p.status, STARKV_EBOUNDS);
-              id = 0;
-            }
-            blk[pg] = id;
-            slot[pg] = t % p.block_size;
+        for (int pg = 0; pg < 8; ++pg) slot[pg] = (t0 + 16 * pg) % p.block_size;
+        // rotary table rows of this tile (+ the 3.2-bit scales of its tokens)
+        ok = !*abort_flag && mbar_wait(&ctl->cs_empty, (item_cnt & 1) ^ 1, abort_flag, p.status);
+        if (ok) {
+          mbar_arrive_expect_tx(&ctl->cs_full, kCsBytes);
+          tma_load_2d(smem + LY::kOffCs, &tm_cs, &ctl->cs_full, 0, t0);
+          tma_load_2d(smem + LY::kOffCs + kCsBytes / 2, &tm_cs, &ctl->cs_full, 64, t0);
+        }
+        if (ok && QUANT) {
+          ok = mbar_wait(&ctl->sc_empty, (item_cnt & 1) ^ 1, abort_flag, p.status);
+          if (ok) {
+            mbar_arrive_expect_tx(&ctl->sc_full, 8 * p.ks_boxes * 2048);
+            for (int pg = 0; pg < 8; ++pg)
+              for (int jb = 0; jb < p.ks_boxes; ++jb)
+                tma_load_3d(smem + LY::kOffScales + (jb * 8 + pg) * 2048, &tm_scales, &ctl->sc_full,
+                            p.ks_x0 + 128 * jb, slot[pg], blk[pg]);
           }
         }
-        // rotary table rows of this tile (+ the 3.2-bit scales of its tokens)
-        if (!mbar_wait(&ctl->cs_empty, (item_cnt & 1) ^ 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(&ctl->cs_full, kCsBytes);
-        tma_load_2d(smem + LY::kOffCs, &tm_cs, &ctl->cs_full, 0, t0);
-        tma_load_2d(smem + LY::kOffCs + kCsBytes / 2, &tm_cs, &ctl->cs_full, 64, t0);
-        if (QUANT) {
-          if (!mbar_wait(&ctl->sc_empty, (item_cnt & 1) ^ 1, abort_flag, p.status)) break;
-          mbar_arrive_expect_tx(&ctl->sc_full, 8 * p.ks_boxes * 2048);
-          for (int pg = 0; pg < 8; ++pg)
-            for (int jb = 0; jb < p.ks_boxes; ++jb)
-              tma_load_3d(smem + LY::kOffScales + (jb * 8 + pg) * 2048, &tm_scales, &ctl->sc_full,
-                          p.ks_x0 + 128 * jb, slot[pg], blk[pg]);
-        }
         const int ab_row0 = (b * p.group + j) * p.k_width;
-        for (int c = 0; c < NC; ++c, ++ab_it, ++code_it) {
+        for (int c = 0; ok && c < NC; ++c, ++ab_it, ++code_it) {
           const int sa = ab_it % kAbSlots;
-          if (!mbar_wait(&ctl->ab_empty[sa], ((ab_it / kAbSlots) & 1) ^ 1, abort_flag, p.status)) break;
+          if (!mbar_wait(&ctl->ab_empty[sa], ((ab_it / kAbSlots) & 1) ^ 1, abort_flag, p.status)) {
+            ok = 0;
+            break;
+          }
           uint8_t* abs = smem + LY::kOffAb + sa * kAbBytes;
           mbar_arrive_expect_tx(&ctl->ab_full[sa], kAbBytes);
           tma_load_2d(abs, &tm_ab, &ctl->ab_full[sa], 0, ab_row0 + c * kChunk);
           tma_load_2d(abs + kAbBytes / 2, &tm_ab, &ctl->ab_full[sa], 64, ab_row0 + c * kChunk);
           const int sc = code_it % LY::kCodeSlots;
-          if (!mbar_wait(&ctl->code_empty[sc], ((code_it / LY::kCodeSlots) & 1) ^ 1, abort_flag, p.status)) break;
+          if (!mbar_wait(&ctl->code_empty[sc], ((code_it / LY::kCodeSlots) & 1) ^ 1, abort_flag, p.status)) {
+            ok = 0;
+            break;
+          }
           uint8_t* cds = smem + LY::kOffCodes + sc * LY::kCodeBytes;
           mbar_arrive_expect_tx(&ctl->code_full[sc], LY::kCodeBytes);
 #pragma unroll
@@ -243,6 +265,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
             }
         }
       }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
     }
   } else if (warp == 1) {
     // ================= MMA issuer =================
@@ -299,7 +322,8 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       if (QUANT && !mbar_wait(&ctl->sc_full, item_cnt & 1, abort_flag, p.status)) break;
       // running sums of the current head: 4 independent chains (bf16: all lanes;
       // 3.2-bit: outlier / inlier lanes, scaled at the flush)
-      float ao[4] = {0.f, 0.f, 0.f, 0.f}, ai[4] = {0.f, 0.f, 0.f, 0.f};
+      float2 ao2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      float2 ai2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       int cur_h = -1;
       auto flush = [&]() {
         float v;
@@ -311,13 +335,13 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
           const uint32_t sw =
               *reinterpret_cast<const uint32_t*>(sb + ((((within >> 4) ^ (sl & 7)) << 4) | (within & 15)));
           const float so = __uint_as_float(sw << 16), si = __uint_as_float(sw & 0xFFFF0000u);
-          v = so * ((ao[0] + ao[1]) + (ao[2] + ao[3])) + si * ((ai[0] + ai[1]) + (ai[2] + ai[3]));
+          v = so * ((ao2[0].x + ao2[0].y) + (ao2[1].x + ao2[1].y)) +
+              si * ((ai2[0].x + ai2[0].y) + (ai2[1].x + ai2[1].y));
         } else {
-          v = (ai[0] + ai[1]) + (ai[2] + ai[3]);
+          v = (ai2[0].x + ai2[0].y) + (ai2[1].x + ai2[1].y);
         }
         atomicAdd(&logits[cur_h * (kTile + 1) + row], v);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ao[i] = ai[i] = 0.f;
+        ao2[0] = ao2[1] = ai2[0] = ai2[1] = make_float2(0.f, 0.f);
       };
       bool ok = true;
       for (int c = 0; c < NC; ++c, ++code_it, ++tb) {
@@ -333,6 +357,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk;
         // this warp's 32-lane groups of the chunk: 2*half and 2*half+1
         const int ng = min(2, max(0, (NT * 16 - c * kChunk - 64 * half + 31) / 32));
+        const int4 m4 = reinterpret_cast<const int4*>(tiles)[c * 2 + half];   // metadata of the 4 lane tiles
         uint32_t zr[2][32];
         if (ng > 0) {
           tmem_ld32_issue(trow + 64 * half, zr[0]);
@@ -344,20 +369,23 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
           const int g = 2 * half + gi;
           if (gi + 1 < ng) tmem_ld32_issue(trow + 32 * (g + 1), zr[1]);
           const uint32_t* z = zr[gi];
-          float x[32];
+          float2 x2[16];   // codes of lanes (2i, 2i+1) of the group
           if (QUANT) {
             // 16 bytes = 32 nibbles: this token's lanes [32g, 32g+32) of the chunk
             const uint8_t* box = codes + pg * LY::kCodeBoxBytes;
             const int phys = g ^ ((sl >> 1) & 3);     // 64-byte swizzle
             const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 64 + phys * 16);
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+            const float2 off8 = make_float2(-8388616.f, -8388616.f);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t lo = w[k] & 0x0F0F0F0Fu, hi = (w[k] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
               for (int bb = 0; bb < 4; ++bb) {
-                x[8 * k + 2 * bb] = nib_f(lo, bb);
-                x[8 * k + 2 * bb + 1] = nib_f(hi, bb);
+                // bytes 0x4B0000nn are the float 2^23 + n; minus 2^23 + 8 gives n - 8
+                const float2 raw = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | bb)),
+                                               __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | bb)));
+                x2[4 * k + bb] = __fadd2_rn(raw, off8);
               }
             }
           } else {
@@ -366,17 +394,20 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
             for (int v = 0; v < 4; ++v) {
               const int phys = ((g & 1) * 4 + v) ^ (sl & 7);   // 128-byte swizzle
               const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 128 + phys * 16);
-              float f[8];
-              if (F16) f16x8_to_f32(u, f); else bf16x8_to_f32(u, f);
+              const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-              for (int i = 0; i < 8; ++i) x[8 * v + i] = f[i];
+              for (int k = 0; k < 4; ++k) {
+                if (F16) {
+                  x2[4 * v + k] = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+                } else {
+                  x2[4 * v + k] = make_float2(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xFFFF0000u));
+                }
+              }
             }
           }
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int tau = ((c * kChunk + 32 * g) >> 4) + hh;
-            if (tau >= NT) break;
-            const int meta = tiles[tau];
+            const int meta = gi == 0 ? (hh == 0 ? m4.x : m4.y) : (hh == 0 ? m4.z : m4.w);
             if (meta < 0) continue;
             const int h = meta & 0xFFFF;
             if (h != cur_h) {
@@ -386,15 +417,23 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
             const int nout = QUANT ? (meta >> 16) & 0xFF : 0;
             if (nout == 0) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) ai[i & 3] = fmaf(x[16 * hh + i], __uint_as_float(z[16 * hh + i]), ai[i & 3]);
+              for (int i = 0; i < 8; ++i) {
+                const float2 zz = make_float2(__uint_as_float(z[16 * hh + 2 * i]), __uint_as_float(z[16 * hh + 2 * i + 1]));
+                ai2[i & 1] = __ffma2_rn(x2[8 * hh + i], zz, ai2[i & 1]);
+              }
             } else if (nout == 16) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) ao[i & 3] = fmaf(x[16 * hh + i], __uint_as_float(z[16 * hh + i]), ao[i & 3]);
+              for (int i = 0; i < 8; ++i) {
+                const float2 zz = make_float2(__uint_as_float(z[16 * hh + 2 * i]), __uint_as_float(z[16 * hh + 2 * i + 1]));
+                ao2[i & 1] = __ffma2_rn(x2[8 * hh + i], zz, ao2[i & 1]);
+              }
             } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float t = x[16 * hh + i] * __uint_as_float(z[16 * hh + i]);
-                if (i < nout) ao[i & 3] += t; else ai[i & 3] += t;
+              for (int i = 0; i < 8; ++i) {
+                const float t0v = x2[8 * hh + i].x * __uint_as_float(z[16 * hh + 2 * i]);
+                const float t1v = x2[8 * hh + i].y * __uint_as_float(z[16 * hh + 2 * i + 1]);
+                if (2 * i < nout) ao2[0].x += t0v; else ai2[0].x += t0v;
+                if (2 * i + 1 < nout) ao2[0].y += t1v; else ai2[0].y += t1v;
               }
             }
           }
