@@ -108,6 +108,22 @@ STARKV_API size_t starkv_decode_workspace_bytes(int32_t n, int32_t num_heads, in
 STARKV_API int starkv_paged_decode_bf16(const StarKVDecodeArgs* args, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/*
+ * No counterpart in the reference. The bf16/f16 decode above for callers that
+ * cannot allocate device memory (a host whose device memory is all handed out
+ * at start-up, or a plug-in inside an engine that owns every allocation): it
+ * takes no workspace and runs in a scratch array built into the library,
+ * STARKV_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held until
+ * the process exits. Calls needing more scratch than that
+ * (starkv_decode_workspace_bytes) return STARKV_EWORKSPACE before any GPU work.
+ * The first call on a device looks the array's address up (with that device
+ * current) and should come before any stream capture. All calls share the
+ * array: calls whose kernels overlap on the GPU race; keep them ordered on one
+ * stream. Its device status word is cleared at the start of each call.
+ */
+#define STARKV_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+STARKV_API int starkv_paged_decode_bf16_noalloc(const StarKVDecodeArgs* args, void* stream);
+
 /* paged_quant.py:357-411 -- 3.2-bit codes (MHA, head_dim 128). */
 STARKV_API int starkv_paged_decode_q32(const StarKVDecodeArgs* args, void* workspace, size_t workspace_bytes,
                             void* stream);
