@@ -24,7 +24,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -45,46 +44,73 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """SM clock and clock-event reasons sampled through NVML by a thread, every
+    millisecond, for as long as the timed region runs (the region is tens of
+    milliseconds, shorter than nvidia-smi's start-up). Samples are also written to
+    gpurun_out/clocks_gpu<i>.csv as a record."""
 
-    def __init__(self, gpu_index: int):
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device):
+        import threading
+        self.samples, self.err = [], None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{device.index or 0}.csv")
         try:
-            self.f = open(self.path, "w")
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}", "--format=csv,noheader",
-                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.p = None
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            try:
+                p = torch_props(device)
+                bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                self.h = N.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = N.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
+        except Exception as e:   # no NVML: reported, not fatal
+            self.err = f"nvml unavailable: {type(e).__name__}"
+            return
+        self.stop_ev = threading.Event()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        N = self.N
+        get_r = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            N.nvmlDeviceGetCurrentClocksThrottleReasons
+        while True:
+            try:
+                self.samples.append((time.perf_counter(), float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)),
+                                     int(get_r(self.h))))
+            except Exception as e:
+                self.err = f"nvml query failed: {type(e).__name__}"
+                return
+            if self.stop_ev.wait(0.001):
+                return
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
+        if self.err and not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err], "samples": 0}
+        self.stop_ev.set()
+        self.t.join(timeout=5)
+        reasons = sorted({nm for _, _, r in self.samples for nm, bit in self.REASONS.items() if r & bit})
         try:
-            self.p.wait(timeout=5)
-        except Exception:
-            self.p.kill()
-        self.f.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1].split()[0]))
-                mx = float(parts[2].split()[0])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            with open(self.path, "w") as f:
+                f.write("t_s,sm_mhz,event_reasons\n")
+                t0 = self.samples[0][0] if self.samples else 0.0
+                for t, mhz, r in self.samples:
+                    f.write(f"{t - t0:.4f},{mhz:.0f},0x{r:x}\n")
+        except OSError:
+            pass
+        sm = [m for _, m, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "source": "nvml, 1 ms"}
+
+
+def torch_props(device):
+    import torch
+    return torch.cuda.get_device_properties(device)
 
 
 # ---------------------------------------------------------------------------
@@ -172,7 +198,7 @@ def measure(layer, device, steps, warmup, dist_on):
             dist.barrier()
         return ms
 
-    clk = Clocks(device.index or 0)
+    clk = Clocks(device)
     ms = timed(step, steps)
     clocks = clk.stop()
 

@@ -75,12 +75,6 @@ __device__ __forceinline__ int find_seq(const int* prefix, int n, int item) {
   return lo;
 }
 
-// n - 8 as float for byte k (0..3) of a word already masked to one nibble per
-// byte: the bytes 0x4B0000nn are the float 2^23 + n.
-__device__ __forceinline__ float nib_f(uint32_t masked, int k) {
-  return __uint_as_float(__byte_perm(masked, 0x4B000000u, 0x7650u | (uint32_t)k)) - 8388616.f;
-}
-
 }  // namespace
 
 size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int ks_boxes) {
