@@ -21,8 +21,8 @@
 // whatever the length mix. A CTA range crossing a sequence boundary flushes its
 // accumulator with f32 atomics into the small L2-resident pv buffer.
 //
-// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 workers (P, dequant,
-// accumulator flush).
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-13 workers (P, dequant,
+// accumulator flush; the three warps of a TMEM lane quarter split the M-tiles).
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
 
@@ -31,6 +31,9 @@ namespace starkv {
 namespace {
 
 constexpr int kMaxStages = 4;
+constexpr int kWorkers = 12;                 // worker warps (3 per TMEM lane quarter)
+constexpr int kWorkerThreads = 32 * kWorkers;
+constexpr int kPvThreads = 64 + kWorkerThreads;
 
 struct PvCtl {
   uint64_t vfull[kMaxStages], vempty[kMaxStages];
@@ -121,7 +124,7 @@ size_t pv_smem_bytes(bool quant, const PvParams& p) {
 }
 
 template <bool QUANT>
-__global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUtensorMap tm_v,
+__global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant__ CUtensorMap tm_v,
                                                     const __grid_constant__ CUtensorMap tm_e, const PvParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -142,12 +145,12 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
     pprefix[p.n] = acc;
     for (int s = 0; s < S; ++s) {
       mbar_init(&ctl->vfull[s], 1);
-      mbar_init(&ctl->vempty[s], QUANT ? 4 : 1);
-      mbar_init(&ctl->pfull[s], 4);
+      mbar_init(&ctl->vempty[s], QUANT ? kWorkers : 1);
+      mbar_init(&ctl->pfull[s], kWorkers);
       mbar_init(&ctl->pempty[s], 1);
     }
     mbar_init(&ctl->accfull, 1);
-    mbar_init(&ctl->accempty, 4);
+    mbar_init(&ctl->accempty, kWorkers);
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -270,8 +273,9 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
     }
   } else {
     // ================= workers: P (+ dequant), accumulator flush =================
-    const int wt = threadIdx.x - 64;     // 0..127
+    const int wt = threadIdx.x - 64;     // 0..kWorkerThreads-1
     const int q = warp & 3;
+    const int wpair = (warp - 2) >> 2;   // which of the kWorkers / 4 warps of lane quarter q
     uint32_t it = 0, acc_cnt = 0;
     int u = u_begin;
     SubItem si;
@@ -288,7 +292,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
       float mseq[4], mt_next[4];
 #pragma unroll
       for (int tk = 0; tk < 4; ++tk) {
-        const int h = min((wt + 128 * tk) >> 2, p.num_heads - 1);
+        const int h = min((wt + kWorkerThreads * tk) >> 2, p.num_heads - 1);
         mseq[tk] = msb[h];
         mt_next[tk] = mtb[(int64_t)h * p.n_tiles + ((si.page0 * 16) >> 7)];
       }
@@ -304,7 +308,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
         // P rows: thread -> (head, 4 consecutive tokens)
 #pragma unroll
         for (int tk = 0; tk < 4; ++tk) {
-          const int task = wt + 128 * tk;
+          const int task = wt + kWorkerThreads * tk;
           if (task >= p.nh * 4) break;
           const int h = task >> 2, kq = task & 3;
           const float mt = mt_next[tk];
@@ -354,7 +358,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
           // chunks with funnel shifts; 8 nibbles -> 4 half2 with the 0x6400 bias trick.
           uint8_t* ab = st + LY.v_bytes;
           const int nvq = p.v_boxes * 8 - 1;    // last staged 16-byte chunk index
-          for (int task = wt; task < nmt * 64; task += 128) {
+          for (int task = wt; task < nmt * 64; task += kWorkerThreads) {
             const int m = task >> 6, tt = task & 63;
             const int k = tt & 15, j = tt >> 4;
             const int gm = mt0 + m;
@@ -428,7 +432,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
           float v = lsum[tk];
           v += __shfl_xor_sync(0xffffffffu, v, 1);
           v += __shfl_xor_sync(0xffffffffu, v, 2);
-          const int task = wt + 128 * tk;
+          const int task = wt + kWorkerThreads * tk;
           const int h = task >> 2;
           if ((task & 3) == 0 && task < p.nh * 4 && h < p.num_heads) atomicAdd(p.l_seq + (int64_t)b * p.num_heads + h, v);
         }
@@ -438,7 +442,7 @@ __global__ void __launch_bounds__(192, 1) pv_kernel(const __grid_constant__ CUte
       tc_fence_after();
       const int row = q * 32 + lane;
       float* pvb = p.pv + (int64_t)b * p.num_heads * p.pv_stride;
-      for (int m = 0; m < nmt; ++m) {
+      for (int m = wpair; m < nmt; m += kWorkers / 4) {
         const int gm = mt0 + m;
         int ch, ch_end;
         if (QUANT) {
@@ -488,9 +492,9 @@ int launch_pv(bool quant, const CUtensorMap& tm_v, const CUtensorMap& tm_e, cons
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return STARKV_ECUDA;
   if (quant)
-    pv_kernel<true><<<num_sms, 192, smem, stream>>>(tm_v, tm_e, p);
+    pv_kernel<true><<<num_sms, kPvThreads, smem, stream>>>(tm_v, tm_e, p);
   else
-    pv_kernel<false><<<num_sms, 192, smem, stream>>>(tm_v, tm_e, p);
+    pv_kernel<false><<<num_sms, kPvThreads, smem, stream>>>(tm_v, tm_e, p);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 

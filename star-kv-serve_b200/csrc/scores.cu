@@ -22,8 +22,8 @@
 //   warp 0      TMA producer: rotary rows, AB chunks (2-slot ring, from L2),
 //               code pages (3-4 slot ring, from HBM) gathered through the block table;
 //   warp 1      MMA issuer, owns the TMEM allocation (4 z buffers x 128 columns);
-//   warps 2-9   epilogue: thread = token row (TMEM lane) x half of the chunk's
-//               columns; per-head partial sums are merged with shared-memory atomics.
+//   warps 2-17  epilogue: thread = token row (TMEM lane) x 32-column group of the
+//               chunk; per-head partial sums are merged with shared-memory atomics.
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
 
@@ -35,8 +35,19 @@ constexpr int kTile = 128;       // tokens per tile (MMA M)
 constexpr int kChunk = 128;      // lanes per chunk (MMA N)
 constexpr int kTmemBufs = 4;
 constexpr int kAbSlots = 2;
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+// Epilogue shape. 3.2-bit codes cost more ALU work per lane (nibble decode and a
+// separate outlier sum) and need more warps to hide latency; bf16 codes are
+// limited by the copy pipeline and do best with fewer, wider threads.
+template <bool QUANT>
+struct Epi {
+  static constexpr int kWarps = QUANT ? 16 : 8;
+  static constexpr int kGroups = kWarps / 4;            // column groups per chunk
+  static constexpr int kSub = kChunk / kGroups / 32;     // 32-column TMEM loads per thread and chunk
+  static constexpr int kThreads = 64 + 32 * kWarps;
+  static constexpr int kTokPerWarp = kTile / kWarps;     // tokens per warp in the statistics phase
+  static_assert(kTokPerWarp % 8 == 0, "statistics phase stores whole 16-byte groups of f16");
+};
+constexpr int kMaxEpiWarps = 16;
 constexpr int kCsBytes = kTile * 128 * 2;       // f16 [128 tokens][128]
 constexpr int kAbBytes = kChunk * 128 * 2;      // f16 [128 lanes][128]
 constexpr int kMaxCodeSlots = 4;
@@ -81,7 +92,7 @@ size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int k
   const int nt = k_width / 16;
   size_t bytes = quant ? Layout<true>::off_logits(ks_boxes) : Layout<false>::off_logits(0);
   bytes += (size_t)num_kv_heads * (kTile + 1) * 4;            // logits [H][129]
-  bytes += (size_t)2 * kEpiWarps * num_kv_heads * 4;          // cross-warp max / sum
+  bytes += (size_t)2 * kMaxEpiWarps * num_kv_heads * 4;       // cross-warp max / sum
   bytes += 16 + (size_t)(nt + 7) / 8 * 8 * 4;                // lane-tile table, padded to whole chunks
   bytes += (size_t)(n + 1) * 4;                               // tile prefix over sequences
   bytes = (bytes + 15) & ~size_t(15);
@@ -90,11 +101,13 @@ size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int k
 }
 
 template <bool QUANT, bool F16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Epi<QUANT>::kThreads, 1)
 scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__ CUtensorMap tm_ab,
               const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
               const ScoresParams p) {
   using LY = Layout<QUANT>;
+  using EP = Epi<QUANT>;
+  constexpr int kEpiWarps = EP::kWarps;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int H = p.num_kv_heads;
@@ -292,10 +305,13 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       }
     }
   } else {
-    // ================= epilogue (warps 2..9) =================
-    const int ew = warp - 2;              // 0..7
+    // ================= epilogue (warps 2 .. 2 + kEpiWarps) =================
+    // Thread = (token row of the tile, column group of the chunk): warp w may only
+    // read TMEM lanes 32 (w % 4) .. +32, so the warps cover the 4 lane quarters x
+    // kGroups column groups of kSub x 32 columns.
+    const int ew = warp - 2;              // 0..kEpiWarps-1
     const int q = warp & 3;               // TMEM lane quarter this warp may access
-    const int half = ew >> 2;             // which 64 columns of each chunk
+    const int gq = ew >> 2;               // column group: chunk columns [32 kSub gq, 32 kSub (gq + 1))
     const int row = q * 32 + lane;        // token within the tile
     const int pg = row >> 4, sl = row & 15;
     uint32_t code_it = 0, tb = 0, item_cnt = 0, epi_phase = 0;
@@ -314,12 +330,16 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int t0 = tile * kTile;
       if (QUANT && !mbar_wait(&ctl->sc_full, item_cnt & 1, abort_flag, p.status)) break;
-      // running sums of the current head: 4 independent chains (bf16: all lanes;
-      // 3.2-bit: outlier / inlier lanes, scaled at the flush)
-      float2 ao2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      float2 ai2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      // running sums of the current head: 4 independent chains over all of its
+      // lanes (ai); 3.2-bit codes also sum the outlier lanes apart (ao), so the
+      // flush applies logit = s_in * ai + (s_out - s_in) * ao.
+      float2 ai[4], ao[2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ai[i] = make_float2(0.f, 0.f);
+      ao[0] = ao[1] = make_float2(0.f, 0.f);
       int cur_h = -1;
       auto flush = [&]() {
+        const float all = ((ai[0].x + ai[0].y) + (ai[1].x + ai[1].y)) + ((ai[2].x + ai[2].y) + (ai[3].x + ai[3].y));
         float v;
         if (QUANT) {
           // (outlier, inlier) bf16 scales of head cur_h for this token
@@ -329,13 +349,15 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
           const uint32_t sw =
               *reinterpret_cast<const uint32_t*>(sb + ((((within >> 4) ^ (sl & 7)) << 4) | (within & 15)));
           const float so = __uint_as_float(sw << 16), si = __uint_as_float(sw & 0xFFFF0000u);
-          v = so * ((ao2[0].x + ao2[0].y) + (ao2[1].x + ao2[1].y)) +
-              si * ((ai2[0].x + ai2[0].y) + (ai2[1].x + ai2[1].y));
+          const float out = (ao[0].x + ao[0].y) + (ao[1].x + ao[1].y);
+          v = si * all + (so - si) * out;
         } else {
-          v = (ai2[0].x + ai2[0].y) + (ai2[1].x + ai2[1].y);
+          v = all;
         }
         atomicAdd(&logits[cur_h * (kTile + 1) + row], v);
-        ao2[0] = ao2[1] = ai2[0] = ai2[1] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ai[i] = make_float2(0.f, 0.f);
+        ao[0] = ao[1] = make_float2(0.f, 0.f);
       };
       bool ok = true;
       for (int c = 0; c < NC; ++c, ++code_it, ++tb) {
@@ -347,91 +369,91 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
           break;
         }
         tc_fence_after();
-        const uint8_t* codes = smem + LY::kOffCodes + sc * LY::kCodeBytes;
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk;
-        // this warp's 32-lane groups of the chunk: 2*half and 2*half+1
-        const int ng = min(2, max(0, (NT * 16 - c * kChunk - 64 * half + 31) / 32));
-        const int4 m4 = reinterpret_cast<const int4*>(tiles)[c * 2 + half];   // metadata of the 4 lane tiles
-        uint32_t zr[2][32];
-        if (ng > 0) {
-          tmem_ld32_issue(trow + 64 * half, zr[0]);
-          tmem_wait(zr[0]);
-        }
+        uint32_t zr[EP::kSub][32];
+        const int nsub = min(EP::kSub, max(0, (NT * 16 - c * kChunk - 32 * EP::kSub * gq + 31) / 32));   // warp-uniform
 #pragma unroll
-        for (int gi = 0; gi < 2; ++gi) {
-          if (gi >= ng) break;
-          const int g = 2 * half + gi;
-          if (gi + 1 < ng) tmem_ld32_issue(trow + 32 * (g + 1), zr[1]);
-          const uint32_t* z = zr[gi];
-          float2 x2[16];   // codes of lanes (2i, 2i+1) of the group
+        for (int sb = 0; sb < EP::kSub; ++sb)
+          if (sb < nsub)
+            tmem_ld32_issue(tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk + 32 * (EP::kSub * gq + sb), zr[sb]);
+#pragma unroll
+        for (int sb = 0; sb < EP::kSub; ++sb) {
+          if (sb >= nsub) break;
+          const int g = EP::kSub * gq + sb;     // 32-lane group of the chunk
+          const uint8_t* codes = smem + LY::kOffCodes + sc * LY::kCodeBytes;
+          // this token's codes of the group's 32 lanes
+          constexpr int kWords = QUANT ? 4 : 16;
+          uint32_t w[kWords];
           if (QUANT) {
-            // 16 bytes = 32 nibbles: this token's lanes [32g, 32g+32) of the chunk
             const uint8_t* box = codes + pg * LY::kCodeBoxBytes;
             const int phys = g ^ ((sl >> 1) & 3);     // 64-byte swizzle
             const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 64 + phys * 16);
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-            const float2 off8 = make_float2(-8388616.f, -8388616.f);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t lo = w[k] & 0x0F0F0F0Fu, hi = (w[k] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-              for (int bb = 0; bb < 4; ++bb) {
-                // bytes 0x4B0000nn are the float 2^23 + n; minus 2^23 + 8 gives n - 8
-                const float2 raw = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | bb)),
-                                               __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | bb)));
-                x2[4 * k + bb] = __fadd2_rn(raw, off8);
-              }
-            }
+            w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
           } else {
             const uint8_t* box = codes + ((g >> 1) * 8 + pg) * LY::kCodeBoxBytes;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int phys = ((g & 1) * 4 + v) ^ (sl & 7);   // 128-byte swizzle
               const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 128 + phys * 16);
-              const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                if (F16) {
-                  x2[4 * v + k] = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-                } else {
-                  x2[4 * v + k] = make_float2(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xFFFF0000u));
-                }
-              }
+              w[4 * v] = u.x; w[4 * v + 1] = u.y; w[4 * v + 2] = u.z; w[4 * v + 3] = u.w;
             }
           }
+          const int2 m2 = reinterpret_cast<const int2*>(tiles)[c * 4 + g];   // metadata of the 2 lane tiles
+          tmem_wait(zr[sb]);   // the first waits for all loads; each names its own registers
+          const uint32_t* z = zr[sb];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int meta = gi == 0 ? (hh == 0 ? m4.x : m4.y) : (hh == 0 ? m4.z : m4.w);
+            const int meta = hh == 0 ? m2.x : m2.y;
             if (meta < 0) continue;
             const int h = meta & 0xFFFF;
             if (h != cur_h) {
               if (cur_h >= 0) flush();
               cur_h = h;
             }
-            const int nout = QUANT ? (meta >> 16) & 0xFF : 0;
-            if (nout == 0) {
+            float2 x2[8];   // codes of lanes (2i, 2i+1) of this 16-lane tile
+            if (QUANT) {
+              const float2 off8 = make_float2(-8388616.f, -8388616.f);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float2 zz = make_float2(__uint_as_float(z[16 * hh + 2 * i]), __uint_as_float(z[16 * hh + 2 * i + 1]));
-                ai2[i & 1] = __ffma2_rn(x2[8 * hh + i], zz, ai2[i & 1]);
-              }
-            } else if (nout == 16) {
+              for (int k = 0; k < 2; ++k) {
+                const uint32_t wd = w[2 * hh + k];
+                const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float2 zz = make_float2(__uint_as_float(z[16 * hh + 2 * i]), __uint_as_float(z[16 * hh + 2 * i + 1]));
-                ao2[i & 1] = __ffma2_rn(x2[8 * hh + i], zz, ao2[i & 1]);
+                for (int bb = 0; bb < 4; ++bb) {
+                  // bytes 0x4B0000nn are the float 2^23 + n; minus 2^23 + 8 gives n - 8
+                  const float2 raw = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | bb)),
+                                                 __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | bb)));
+                  x2[4 * k + bb] = __fadd2_rn(raw, off8);
+                }
               }
             } else {
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const float t0v = x2[8 * hh + i].x * __uint_as_float(z[16 * hh + 2 * i]);
-                const float t1v = x2[8 * hh + i].y * __uint_as_float(z[16 * hh + 2 * i + 1]);
-                if (2 * i < nout) ao2[0].x += t0v; else ai2[0].x += t0v;
-                if (2 * i + 1 < nout) ao2[0].y += t1v; else ai2[0].y += t1v;
+                const uint32_t wd = w[8 * hh + i];
+                if (F16)
+                  x2[i] = __half22float2(*reinterpret_cast<const __half2*>(&wd));
+                else
+                  x2[i] = make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xFFFF0000u));
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float2 zz = make_float2(__uint_as_float(z[16 * hh + 2 * i]), __uint_as_float(z[16 * hh + 2 * i + 1]));
+              ai[i & 3] = __ffma2_rn(x2[i], zz, ai[i & 3]);
+            }
+            if (QUANT) {
+              const int nout = (meta >> 16) & 0xFF;   // outlier lanes lead the head's first tile
+              if (nout > 0) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float2 zz =
+                      make_float2(__uint_as_float(z[16 * hh + 2 * i]), __uint_as_float(z[16 * hh + 2 * i + 1]));
+                  if (2 * i + 1 < nout)
+                    ao[i & 1] = __ffma2_rn(x2[i], zz, ao[i & 1]);
+                  else if (2 * i < nout)
+                    ao[0].x = fmaf(x2[i].x, zz.x, ao[0].x);
+                }
               }
             }
           }
-          if (gi + 1 < ng) tmem_wait(zr[1]);
         }
         tc_fence_before();
         __syncwarp();
@@ -446,12 +468,13 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         if (lane == 0) mbar_arrive(&ctl->sc_empty);
       }
       if (!ok || !epi_sync()) break;
-      // ---- per-head tile softmax statistics: warp ew owns tokens [16 ew, 16 ew + 16) ----
+      // ---- per-head tile softmax statistics: warp ew owns kTokPerWarp tokens ----
+      constexpr int kTokPerWarp = EP::kTokPerWarp;
       for (int h = lane; h < H; h += 32) {
         float m = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int t = 16 * ew + i;
+        for (int i = 0; i < kTokPerWarp; ++i) {
+          const int t = kTokPerWarp * ew + i;
           if (t0 + t < L) m = fmaxf(m, logits[h * (kTile + 1) + t]);
         }
         red_m[ew * H + h] = m;
@@ -462,18 +485,18 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         for (int w2 = 1; w2 < kEpiWarps; ++w2) m = fmaxf(m, red_m[w2 * H + h]);
         const int hq = h * p.group + j;
         float ssum = 0.f;
-        __align__(16) __half ev[16];
+        __align__(16) __half ev[kTokPerWarp];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int t = 16 * ew + i;
+        for (int i = 0; i < kTokPerWarp; ++i) {
+          const int t = kTokPerWarp * ew + i;
           float v = 0.f;
           if (t0 + t < L) v = __expf(logits[h * (kTile + 1) + t] - m);
           ssum += v;
           ev[i] = __float2half_rn(v);
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + 16 * ew);
-        dst[0] = reinterpret_cast<const uint4*>(ev)[0];
-        dst[1] = reinterpret_cast<const uint4*>(ev)[1];
+        uint4* dst = reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + kTokPerWarp * ew);
+#pragma unroll
+        for (int i = 0; i < kTokPerWarp / 8; ++i) dst[i] = reinterpret_cast<const uint4*>(ev)[i];
         red_l[ew * H + h] = ssum;
       }
       if (!epi_sync()) break;
@@ -517,11 +540,11 @@ int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab
     return STARKV_ECUDA;
   const int grid = num_sms;
   if (quant)
-    scores_kernel<true, false><<<grid, kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
+    scores_kernel<true, false><<<grid, Epi<true>::kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
   else if (f16)
-    scores_kernel<false, true><<<grid, kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
+    scores_kernel<false, true><<<grid, Epi<false>::kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
   else
-    scores_kernel<false, false><<<grid, kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
+    scores_kernel<false, false><<<grid, Epi<false>::kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 
