@@ -94,7 +94,7 @@ Workspace workspace_layout(int n, int num_heads, int num_kv_heads, int k_width, 
   w.l_pad = w.n_tiles * 128;
   size_t off = 0;
   w.status = off; off += 256;
-  w.ab = off; off = align256(off + (size_t)n * group * k_width * 128 * 2);
+  w.ab = off; off = align256(off + (size_t)n * group * ((k_width + 127) / 128) * 128 * 128 * 2);   // MMA image
   w.cs = off; off = align256(off + (size_t)w.l_pad * 128 * 2);
   w.e16 = off; off = align256(off + (size_t)n * num_heads * w.l_pad * 2);
   w.m_tile = off; off = align256(off + (size_t)n * num_heads * w.n_tiles * 4);
@@ -155,39 +155,69 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   float* pv = reinterpret_cast<float*>(W + ws.pv);
 
   // ---- TMA descriptors ----
-  CUtensorMap tm_cs, tm_ab, tm_codes, tm_wide;
+  CUtensorMap tm_cs, tm_ab, tm_code, tm_tail, tm_sc, tm_v;
+  // Rotary rows and AB are written by the fold kernel as ready-made 128-byte-swizzled
+  // MMA tiles; they are copied as 2 KB rows (8-byte elements, no swizzle): one box
+  // per 32 KB rotary tile, one per 16 KB half-chunk of AB.
+  const int ncp = (a->k_width + 127) / 128;
   {
-    const uint64_t dims[2] = {128, (uint64_t)ws.l_pad};
-    const uint64_t str[1] = {256};
-    const uint32_t box[2] = {64, 128};
-    if ((st = make_map(&tm_cs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cs16, dims, str, box,
-                       CU_TENSOR_MAP_SWIZZLE_128B)))
+    const uint64_t dims[2] = {256, (uint64_t)ws.n_tiles * 16};
+    const uint64_t str[1] = {2048};
+    const uint32_t box[2] = {256, 16};
+    if ((st = make_map(&tm_cs, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, cs16, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
   }
   {
-    const uint64_t dims[2] = {128, (uint64_t)a->n * group * a->k_width};
-    const uint64_t str[1] = {256};
-    const uint32_t box[2] = {64, 128};
-    if ((st = make_map(&tm_ab, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ab, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)))
+    const uint64_t dims[2] = {256, (uint64_t)a->n * group * ncp * 2 * 8};
+    const uint64_t str[1] = {2048};
+    const uint32_t box[2] = {256, 8};
+    if ((st = make_map(&tm_ab, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, ab, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
   }
   const int es = quant ? 1 : 2;
   const uint64_t row_elems = quant ? (uint64_t)a->row_nbytes : (uint64_t)(a->k_width + a->v_rank);
   if (a->cache_stride[1] < (int64_t)row_elems || a->cache_stride[0] < a->cache_stride[1] * a->block_size)
     return STARKV_EINVAL;
+  // P.V: V code tiles straight from the cache (bf16: 64 channels = 128 B per box,
+  // 128-byte swizzle, the MMA's A layout; 3.2-bit: 128-byte boxes of V bytes).
   {
     const uint64_t dims[3] = {row_elems, (uint64_t)a->block_size, (uint64_t)a->num_blocks};
     const uint64_t str[2] = {(uint64_t)a->cache_stride[1] * es, (uint64_t)a->cache_stride[0] * es};
     const CUtensorMapDataType dt = quant ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
-    const uint32_t box[3] = {64, 16, 1};   // bf16: 64 lanes = 128 B; 3.2-bit: 64 B = 128 lanes
-    if ((st = make_map(&tm_codes, dt, 3, a->kv_cache, dims, str, box,
-                       quant ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
+    const uint32_t box[3] = {quant ? 128u : 64u, 16, 1};
+    if ((st = make_map(&tm_v, dt, 3, a->kv_cache, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  // Scores: code windows cut from an 8-byte-element view of the cache, unswizzled,
+  // with the row pitch the kernel stages them at (an odd multiple of 16 bytes).
+  int code_pitch = 0, tail_pitch = 0, n_wins = 0, sc_pitch = 0, sc_x0 = 0;
+  {
+    const uint64_t row_bytes = row_elems * es;
+    if (row_bytes % 8) return STARKV_EALIGN;
+    const int win_bytes = scores_window_bytes(quant);
+    const int win_lanes = quant ? 2 * win_bytes : win_bytes / 2;
+    n_wins = (a->k_width + win_lanes - 1) / win_lanes;
+    const int tail_lanes = (a->k_width - (n_wins - 1) * win_lanes + 31) & ~31;   // whole 32-lane groups
+    code_pitch = code_pitch_bytes(win_bytes);
+    tail_pitch = code_pitch_bytes(quant ? tail_lanes / 2 : tail_lanes * 2);
+    const uint64_t dims[3] = {row_bytes / 8, (uint64_t)a->block_size, (uint64_t)a->num_blocks};
+    const uint64_t str[2] = {(uint64_t)a->cache_stride[1] * es, (uint64_t)a->cache_stride[0] * es};
+    const uint32_t box[3] = {(uint32_t)code_pitch / 8, 16, 1};
+    const uint32_t box_t[3] = {(uint32_t)tail_pitch / 8, 16, 1};
+    if ((st = make_map(&tm_code, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, a->kv_cache, dims, str, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
+    if ((st = make_map(&tm_tail, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, a->kv_cache, dims, str, box_t,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
+    tm_sc = tm_code;
     if (quant) {
-      const uint32_t box2[3] = {128, 16, 1};   // scale / V byte boxes
-      if ((st = make_map(&tm_wide, dt, 3, a->kv_cache, dims, str, box2, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-    } else {
-      tm_wide = tm_codes;
+      sc_x0 = a->ks_off & ~15;
+      sc_pitch = code_pitch_bytes(a->ks_off + 4 * a->num_kv_heads - sc_x0);
+      if (sc_pitch / 8 > 256) return STARKV_EINVAL;
+      const uint32_t box_s[3] = {(uint32_t)sc_pitch / 8, 16, 1};
+      if ((st = make_map(&tm_sc, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, a->kv_cache, dims, str, box_s,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
     }
   }
 
@@ -199,7 +229,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   fp.head_of_lane = quant ? a->head_of_lane : nullptr;
   fp.k_ranks = a->k_ranks; fp.k_head_offsets = a->k_head_offsets;
   fp.n = a->n; fp.num_heads = a->num_heads; fp.num_kv_heads = a->num_kv_heads; fp.group = group;
-  fp.k_width = a->k_width; fp.head_dim = a->head_dim; fp.scale = a->scale; fp.ab = ab;
+  fp.k_width = a->k_width; fp.head_dim = a->head_dim; fp.scale = a->scale; fp.ab = ab; fp.ab_image = 1;
   fp.cs = a->cos_sin_cache; fp.cs_s0 = a->cs_stride[0]; fp.cs_s1 = a->cs_stride[1]; fp.cs_dtype = a->cs_dtype;
   fp.cs_rows = a->cs_rows; fp.cs16 = cs16; fp.l_pad = ws.l_pad; fp.max_seq_len = a->max_seq_len;
   fp.m_seq = m_seq; fp.l_seq = l_seq; fp.m_count = a->n * a->num_heads;
@@ -220,15 +250,12 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   sp.max_seq_len = a->max_seq_len; sp.cache_dtype = a->cache_dtype;
   sp.k_ranks = a->k_ranks; sp.k_head_offsets = a->k_head_offsets;
   sp.tile_head = a->tile_head; sp.tile_nout = a->tile_nout; sp.tile_last = a->tile_last;
-  if (quant) {
-    sp.ks_off = a->ks_off;
-    sp.ks_x0 = a->ks_off & ~15;
-    sp.ks_boxes = (a->ks_off + 4 * a->num_kv_heads - sp.ks_x0 + 127) / 128;
-    if (sp.ks_boxes > 3) return STARKV_EINVAL;
-  }
+  if (quant) sp.ks_off = a->ks_off;
+  sp.code_pitch = code_pitch; sp.tail_pitch = tail_pitch; sp.n_wins = n_wins;
+  sp.sc_pitch = sc_pitch; sp.sc_x0 = sc_x0;
   sp.e16 = e16; sp.m_tile = m_tile; sp.m_seq = m_seq;
   sp.l_pad = ws.l_pad; sp.n_tiles = ws.n_tiles; sp.status = status;
-  if ((st = launch_scores(quant, tm_cs, tm_ab, tm_codes, tm_wide, sp, dev.sms, stream))) return st;
+  if ((st = launch_scores(quant, tm_cs, tm_ab, tm_code, tm_tail, tm_sc, sp, dev.sms, stream))) return st;
   if (pev) cudaEventRecord(pev[2], stream);
 
   // ---- P.V ----
@@ -273,7 +300,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
     if ((st = make_map(&tm_e, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e16, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
   }
-  if ((st = launch_pv(quant, tm_wide, tm_e, pp, dev.sms, stream))) return st;
+  if ((st = launch_pv(quant, tm_v, tm_e, pp, dev.sms, stream))) return st;
   if (pev) cudaEventRecord(pev[3], stream);
 
   // ---- lift ----

@@ -78,20 +78,32 @@ __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fol
         bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
       }
     }
-    __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
-    *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
-    *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
+    if (p.ab_image) {
+      // the 128-byte-swizzled K-major tile the score MMA reads as its B operand
+      const int nc = (p.k_width + 127) / 128;
+      const int c = r >> 7, half = (r >> 6) & 1, i = r & 63;
+      __half* blk = p.ab + ((((int64_t)bj * nc + c) * 2 + half) << 13);   // 8192 halves per block
+      const int unit = (threadIdx.x & 7) ^ (i & 7);
+      *reinterpret_cast<uint4*>(blk + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(av);
+      *reinterpret_cast<uint4*>(blk + 4096 + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(bv);
+    } else {
+      __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
+      *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
+      *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
+    }
     return;
   }
   if (bid < n_fold_blocks + n_cs_blocks) {
-    // rotary table rows -> f16, zero past the table / max_seq_len
+    // rotary table rows -> f16 (zero past the table / max_seq_len), written as the
+    // 128-byte-swizzled K-major tiles the score MMA reads as its A operand
     const int64_t e = (int64_t)(bid - n_fold_blocks) * 128 + threadIdx.x;
     const int64_t row = e >> 7;
     const int col = (int)(e & 127);
     if (row >= p.l_pad) return;
     float v = 0.f;
     if (row < p.cs_rows && row < p.max_seq_len) v = load_elem(p.cs, row * p.cs_s0 + col * p.cs_s1, p.cs_dtype);
-    p.cs16[e] = __float2half_rn(v);
+    const int t = (int)(row & 127), kh = col >> 6, unit = ((col & 63) >> 3) ^ (t & 7);
+    p.cs16[((row >> 7) << 14) + kh * 8192 + t * 64 + unit * 8 + (col & 7)] = __float2half_rn(v);
     return;
   }
   // init: sequence max = -inf, pv = 0

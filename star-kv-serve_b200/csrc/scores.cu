@@ -8,21 +8,39 @@
 // [W, 128] per sequence),
 //     logit[t, h] = sum_{r in head h} x[t, r] * z[t, r],   z = CS[t, :] . AB[r, :]
 // where CS[t] = [cos_t | sin_t] is row t of the rotary table. z is a dense
-// [128 tokens x 128 lanes] x K=128 contraction per chunk of lanes: it runs on
-// the tcgen05 tensor core (M=128 tokens, N=128 lanes, K=128, f16 in, f32 out in
-// TMEM). The codes x are only used elementwise in the epilogue, so the 4-bit
-// cache is dequantized in registers ((n - 8) * bf16 scale, bit-exact) and never
-// has to be laid out as an MMA operand.
+// [tokens x 128 lanes] x K=128 contraction per chunk of lanes; the codes x are
+// only used elementwise in the epilogue, so the 4-bit cache is dequantized in
+// registers ((n - 8) * bf16 scale, bit-exact) and never has to be laid out as an
+// MMA operand.
 //
-// Per tile (one sequence, 128 tokens) the epilogue reduces each head's logits
-// to (tile max m, tile sum l = sum exp(logit - m)) and stores exp(logit - m) as
-// f16 ("e16"); the P.V kernel rescales by exp(m - M) with M the sequence max.
+// CTA pairs. Every tile of 128 tokens needs the whole AB of its sequence (W x 256 B,
+// ~350 KB), which makes AB, re-read from L2, as large as the codes themselves. Two
+// CTAs on neighbouring SMs therefore form a cluster and run one tcgen05.mma with
+// cta_group::2 (M = 256 tokens, N = 128 lanes, K = 128): each CTA stages the rotary
+// rows of its own 128 tokens (A) and HALF of every AB chunk (B, 64 lanes), so AB is
+// read once per 256 tokens. CTA 0 issues the MMAs; the peer's TMA completions and
+// its epilogue's buffer releases are counted on CTA 0's barriers, and each MMA
+// completion is multicast to the barriers of both CTAs.
 //
-// Persistent CTAs (one per SM), warp roles:
-//   warp 0      TMA producer: rotary rows, AB chunks (2-slot ring, from L2),
-//               code pages (3-4 slot ring, from HBM) gathered through the block table;
-//   warp 1      MMA issuer, owns the TMEM allocation (4 z buffers x 128 columns);
-//   warps 2-17  epilogue: thread = token row (TMEM lane) x 32-column group of the
+// Code staging. A tile's codes are read window by window (512 B of each row for
+// bf16 codes, 384 B for 3.2-bit codes), one TMA box of 16 rows per page. Boxes of
+// 128-byte rows cap the copy engine well below the HBM peak when every page is
+// visited once per window; rows of 384-512 B stream near it. The boxes are cut from
+// an 8-byte-element view of the cache without swizzling, 16 bytes wider than the
+// window when needed so that the row pitch in shared memory is an odd multiple of
+// 16 bytes: the epilogue's 16-byte reads of 8 consecutive token rows then fall in
+// 8 different bank groups.
+//
+// Per tile the epilogue reduces each head's logits to the tile max m and stores
+// exp(logit - m) as f16 ("e16"); the P.V kernel rescales by exp(m - M) with M the
+// sequence max.
+//
+// Persistent CTA pairs, warp roles in each CTA:
+//   warp 0      TMA producer: rotary rows and AB halves (into this CTA, counted on
+//               CTA 0's barriers), code windows and 3.2-bit scales (2-slot rings,
+//               from HBM) gathered through the block table;
+//   warp 1      TMEM owner (pair allocation, all 512 columns); in CTA 0 also the MMA issuer;
+//   warps 2-17  epilogue: thread = token row (TMEM lane) x 32-lane group of the
 //               chunk; per-head partial sums are merged with shared-memory atomics.
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
@@ -31,51 +49,62 @@ namespace starkv {
 
 namespace {
 
-constexpr int kTile = 128;       // tokens per tile (MMA M)
-constexpr int kChunk = 128;      // lanes per chunk (MMA N)
-constexpr int kTmemBufs = 4;
-constexpr int kAbSlots = 2;
-// Epilogue shape. 3.2-bit codes cost more ALU work per lane (nibble decode and a
-// separate outlier sum) and need more warps to hide latency; bf16 codes are
-// limited by the copy pipeline and do best with fewer, wider threads.
-template <bool QUANT>
-struct Epi {
-  static constexpr int kWarps = QUANT ? 16 : 8;
-  static constexpr int kGroups = kWarps / 4;            // column groups per chunk
-  static constexpr int kSub = kChunk / kGroups / 32;     // 32-column TMEM loads per thread and chunk
-  static constexpr int kThreads = 64 + 32 * kWarps;
-  static constexpr int kTokPerWarp = kTile / kWarps;     // tokens per warp in the statistics phase
-  static_assert(kTokPerWarp % 8 == 0, "statistics phase stores whole 16-byte groups of f16");
-};
-constexpr int kMaxEpiWarps = 16;
+constexpr int kTile = 128;       // tokens per CTA and tile (MMA M / 2)
+constexpr int kPairTokens = 2 * kTile;
+constexpr int kChunk = 128;      // lanes per MMA (N)
+constexpr int kHalfLanes = kChunk / 2;   // AB lanes staged by each CTA of the pair
+constexpr int kCodeSlots = 2;
 constexpr int kCsBytes = kTile * 128 * 2;       // f16 [128 tokens][128]
-constexpr int kAbBytes = kChunk * 128 * 2;      // f16 [128 lanes][128]
-constexpr int kMaxCodeSlots = 4;
+constexpr int kAbBytes = kHalfLanes * 128 * 2;  // f16 [64 lanes][128] per CTA
+constexpr int kTmemCols = 512;
+constexpr int kTmemBufs = kTmemCols / kChunk;
+constexpr int kGroups = kChunk / 32;            // 32-lane groups per chunk
+constexpr int kEpiWarps = 4 * kGroups;          // 4 TMEM lane quarters x groups
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kTokPerWarp = kTile / kEpiWarps;  // tokens per warp in the statistics phase
+constexpr int kMaxAbSlots = 3;
 
 template <bool QUANT>
-struct Layout {
-  // bf16 codes: 2 boxes of 64 lanes (128 B) per page; 3.2-bit codes: one box of
-  // 64 bytes (128 lanes) per page.
-  static constexpr int kCodeSlots = QUANT ? 4 : 3;
-  static constexpr int kCodeBoxes = QUANT ? 1 : 2;
-  static constexpr int kCodeBoxBytes = QUANT ? 16 * 64 : 16 * 128;
-  static constexpr int kCodeBytes = 8 * kCodeBoxes * kCodeBoxBytes;   // per slot (8 pages)
-  static constexpr int kOffCs = 0;
-  static constexpr int kOffAb = kOffCs + kCsBytes;
-  static constexpr int kOffCodes = kOffAb + kAbSlots * kAbBytes;
-  static constexpr int kOffScales = kOffCodes + kCodeSlots * kCodeBytes;   // 3.2-bit scale boxes
-  static __host__ __device__ int off_logits(int ks_boxes) { return kOffScales + ks_boxes * 8 * 2048; }
+struct Cfg {
+  static constexpr int kAbSlots = QUANT ? 3 : 2;
+  static constexpr int kWinLanes = QUANT ? 768 : 256;        // lanes per code window
+  static constexpr int kWinBytes = QUANT ? kWinLanes / 2 : kWinLanes * 2;
+  static constexpr int kChunksPerWin = kWinLanes / kChunk;
 };
 
 struct SharedCtl {
-  uint64_t ab_full[kAbSlots], ab_empty[kAbSlots];
-  uint64_t code_full[kMaxCodeSlots], code_empty[kMaxCodeSlots];
+  uint64_t ab_full[kMaxAbSlots], ab_empty[kMaxAbSlots];
+  uint64_t code_full[kCodeSlots], code_empty[kCodeSlots];
   uint64_t cs_full, cs_empty, sc_full, sc_empty;
   uint64_t tfull[kTmemBufs], tempty[kTmemBufs];
   uint64_t epi;            // bounded barrier among the epilogue warps
   uint32_t tmem_base;
   int abort_flag;
 };
+
+// Shared memory carve-up (byte offsets from the 1024-aligned base).
+struct SmemLayout {
+  int cs, ab, codes, code_slot, sc, logits, red, tiles, prefix, ctl, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int k_width, int code_pitch,
+                                                  int sc_pitch) {
+  SmemLayout L;
+  const int ab_slots = quant ? Cfg<true>::kAbSlots : Cfg<false>::kAbSlots;
+  const int nc = (k_width + kChunk - 1) / kChunk;
+  L.cs = 0;
+  L.ab = L.cs + kCsBytes;
+  L.codes = L.ab + ab_slots * kAbBytes;
+  L.code_slot = (kTile * code_pitch + 127) & ~127;
+  L.sc = L.codes + kCodeSlots * L.code_slot;
+  L.logits = L.sc + (quant ? (kTile * sc_pitch + 127) & ~127 : 0);
+  L.red = L.logits + H * (kTile + 1) * 4;
+  L.tiles = (L.red + kEpiWarps * H * 4 + 15) & ~15;
+  L.prefix = L.tiles + nc * (kChunk / 16) * 4;
+  L.ctl = (L.prefix + (n + 1) * 4 + 15) & ~15;
+  L.total = L.ctl + (int)sizeof(SharedCtl);
+  return L;
+}
 
 __device__ __forceinline__ int find_seq(const int* prefix, int n, int item) {
   int lo = 0, hi = n;  // prefix[lo] <= item < prefix[hi]
@@ -88,44 +117,44 @@ __device__ __forceinline__ int find_seq(const int* prefix, int n, int item) {
 
 }  // namespace
 
-size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int ks_boxes) {
-  const int nt = k_width / 16;
-  size_t bytes = quant ? Layout<true>::off_logits(ks_boxes) : Layout<false>::off_logits(0);
-  bytes += (size_t)num_kv_heads * (kTile + 1) * 4;            // logits [H][129]
-  bytes += (size_t)2 * kMaxEpiWarps * num_kv_heads * 4;       // cross-warp max / sum
-  bytes += 16 + (size_t)(nt + 7) / 8 * 8 * 4;                // lane-tile table, padded to whole chunks
-  bytes += (size_t)(n + 1) * 4;                               // tile prefix over sequences
-  bytes = (bytes + 15) & ~size_t(15);
-  bytes += sizeof(SharedCtl) + 1024;                          // control + alignment slack
-  return bytes;
+// Row pitch (bytes) of a staged code window of `bytes` bytes: rounded up to 16 and,
+// if needed, one more 16 so that pitch / 16 is odd.
+int code_pitch_bytes(int bytes) {
+  int p = (bytes + 15) & ~15;
+  if (((p >> 4) & 1) == 0) p += 16;
+  return p;
+}
+
+int scores_window_bytes(bool quant) { return quant ? Cfg<true>::kWinBytes : Cfg<false>::kWinBytes; }
+
+size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch) {
+  return (size_t)smem_layout(quant, num_kv_heads, n, k_width, code_pitch, sc_pitch).total + 1024;
 }
 
 template <bool QUANT, bool F16>
-__global__ void __launch_bounds__(Epi<QUANT>::kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__ CUtensorMap tm_ab,
-              const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
-              const ScoresParams p) {
-  using LY = Layout<QUANT>;
-  using EP = Epi<QUANT>;
-  constexpr int kEpiWarps = EP::kWarps;
+              const __grid_constant__ CUtensorMap tm_code, const __grid_constant__ CUtensorMap tm_tail,
+              const __grid_constant__ CUtensorMap tm_sc, const ScoresParams p) {
+  using C = Cfg<QUANT>;
+  constexpr int kAbSlots = C::kAbSlots;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int H = p.num_kv_heads;
   const int NT = p.k_width / 16;
   const int NC = (p.k_width + kChunk - 1) / kChunk;
-  const int ks_boxes = QUANT ? p.ks_boxes : 0;
-  float* logits = reinterpret_cast<float*>(smem + LY::off_logits(ks_boxes));   // [H][129]
-  float* red_m = logits + H * (kTile + 1);                                      // [8][H]
-  float* red_l = red_m + kEpiWarps * H;                                         // [8][H]
-  int* tiles = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(red_l + kEpiWarps * H) + 15) &
-                                      ~uintptr_t(15));                          // [NC * 8], -1 past NT
-  int* prefix = tiles + NC * 8;                                                 // [n+1]
-  SharedCtl* ctl =
-      reinterpret_cast<SharedCtl*>((reinterpret_cast<uintptr_t>(prefix + p.n + 1) + 15) & ~uintptr_t(15));
+  const SmemLayout SL = smem_layout(QUANT, H, p.n, p.k_width, p.code_pitch, p.sc_pitch);
+  float* logits = reinterpret_cast<float*>(smem + SL.logits);    // [H][129]
+  float* red_m = reinterpret_cast<float*>(smem + SL.red);        // [warps][H]
+  int* tiles = reinterpret_cast<int*>(smem + SL.tiles);           // [NC * 8], -1 past NT
+  int* prefix = reinterpret_cast<int*>(smem + SL.prefix);         // [n+1]
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem + SL.ctl);
   volatile int* abort_flag = &ctl->abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();           // 0: issues the pair's MMAs
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
   // ---- prologue: tables, zeroed logits, barriers, TMEM ----
   if (threadIdx.x == 0) {
@@ -133,11 +162,11 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     for (int b = 0; b < p.n; ++b) {
       prefix[b] = acc;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
-      acc += (L + kTile - 1) / kTile * p.group;
+      acc += (L + kPairTokens - 1) / kPairTokens * p.group;
     }
     prefix[p.n] = acc;
   }
-  for (int t = threadIdx.x; t < NC * 8; t += blockDim.x) {
+  for (int t = threadIdx.x; t < NC * (kChunk / 16); t += blockDim.x) {
     int entry = -1;   // head | outlier lanes << 16 (3.2-bit)
     if (t >= NT) {
     } else if (QUANT) {
@@ -157,11 +186,13 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
   }
   for (int i = threadIdx.x; i < H * (kTile + 1); i += blockDim.x) logits[i] = 0.f;
   if (threadIdx.x == 0) {
+    // In CTA 0, ab_full / cs_full count the TMA bytes of BOTH CTAs and tempty the
+    // epilogue warps of both; the peer's own copies of those barriers stay unused.
     for (int s = 0; s < kAbSlots; ++s) {
       mbar_init(&ctl->ab_full[s], 1);
       mbar_init(&ctl->ab_empty[s], 1);
     }
-    for (int s = 0; s < LY::kCodeSlots; ++s) {
+    for (int s = 0; s < kCodeSlots; ++s) {
       mbar_init(&ctl->code_full[s], 1);
       mbar_init(&ctl->code_empty[s], kEpiWarps);
     }
@@ -171,35 +202,37 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     mbar_init(&ctl->sc_empty, kEpiWarps);
     for (int i = 0; i < kTmemBufs; ++i) {
       mbar_init(&ctl->tfull[i], 1);
-      mbar_init(&ctl->tempty[i], kEpiWarps);
+      mbar_init(&ctl->tempty[i], 2 * kEpiWarps);
     }
     mbar_init(&ctl->epi, 32 * kEpiWarps);
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(&ctl->tmem_base, kTmemBufs * kChunk);
+  if (warp == 1) tmem_alloc_pair(&ctl->tmem_base, kTmemCols);
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();   // both CTAs' barriers and TMEM exist before any remote use
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   const int total_items = prefix[p.n];
 
   if (warp == 0) {
-    // ================= TMA producer =================
-    // Lanes 0-7 fetch the 8 block ids of the NEXT tile while lane 0 issues the
-    // current tile's copies, so the block table's latency stays off the issue path.
+    // ================= TMA producer (both CTAs) =================
+    // Lanes 0-7 fetch the 8 block ids of this CTA's half of the NEXT item while
+    // lane 0 issues the current copies, so the block table's latency stays off the
+    // issue path.
     if (lane == 0) {
       tma_prefetch(&tm_cs);
       tma_prefetch(&tm_ab);
-      tma_prefetch(&tm_codes);
-      if (QUANT) tma_prefetch(&tm_scales);
+      tma_prefetch(&tm_code);
+      tma_prefetch(&tm_tail);
+      if (QUANT) tma_prefetch(&tm_sc);
     }
     auto block_of = [&](int item) -> int {   // block id of page `lane` of an item (lanes 0-7)
       if (item >= total_items || lane >= 8) return 0;
       const int b = find_seq(prefix, p.n, item);
-      const int tile = (item - prefix[b]) / p.group;
+      const int sup = (item - prefix[b]) / p.group;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
-      const int t = tile * kTile + 16 * lane;
+      const int t = sup * kPairTokens + kTile * (int)rank + 16 * lane;
       if (t >= L) return 0;
       const int col = t / p.block_size;
       int id = -1;
@@ -210,11 +243,13 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       }
       return id;
     };
+    const int win_u64 = C::kWinBytes / 8;
+    const uint32_t cs_full_l = leader_addr(&ctl->cs_full);
     uint32_t ab_it = 0, code_it = 0, item_cnt = 0;
-    int ids_next = block_of(blockIdx.x);
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++item_cnt) {
+    int ids_next = block_of(pair);
+    for (int item = pair; item < total_items; item += n_pairs, ++item_cnt) {
       const int ids = ids_next;
-      ids_next = block_of(item + gridDim.x);
+      ids_next = block_of(item + n_pairs);
       int blk[8], slot[8];
 #pragma unroll
       for (int pg = 0; pg < 8; ++pg) blk[pg] = __shfl_sync(0xffffffffu, ids, pg);
@@ -223,64 +258,75 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         const int b = find_seq(prefix, p.n, item);
         const int rem = item - prefix[b];
         const int j = rem % p.group;
-        const int tile = rem / p.group;
-        const int t0 = tile * kTile;
+        const int t0 = (rem / p.group) * kPairTokens + kTile * (int)rank;   // this CTA's first token
 #pragma unroll
         for (int pg = 0; pg < 8; ++pg) slot[pg] = (t0 + 16 * pg) % p.block_size;
-        // rotary table rows of this tile (+ the 3.2-bit scales of its tokens)
+        // rotary rows of this CTA's tokens: the pair MMA's A half
         ok = !*abort_flag && mbar_wait(&ctl->cs_empty, (item_cnt & 1) ^ 1, abort_flag, p.status);
         if (ok) {
-          mbar_arrive_expect_tx(&ctl->cs_full, kCsBytes);
-          tma_load_2d(smem + LY::kOffCs, &tm_cs, &ctl->cs_full, 0, t0);
-          tma_load_2d(smem + LY::kOffCs + kCsBytes / 2, &tm_cs, &ctl->cs_full, 64, t0);
+          if (rank == 0) mbar_arrive_expect_tx(&ctl->cs_full, 2 * kCsBytes);
+          tma_load_2d_pair(smem + SL.cs, &tm_cs, cs_full_l, 0, (t0 / kTile) * 16);   // one 32 KB tile image
         }
         if (ok && QUANT) {
           ok = mbar_wait(&ctl->sc_empty, (item_cnt & 1) ^ 1, abort_flag, p.status);
           if (ok) {
-            mbar_arrive_expect_tx(&ctl->sc_full, 8 * p.ks_boxes * 2048);
+            mbar_arrive_expect_tx(&ctl->sc_full, kTile * p.sc_pitch);
             for (int pg = 0; pg < 8; ++pg)
-              for (int jb = 0; jb < p.ks_boxes; ++jb)
-                tma_load_3d(smem + LY::kOffScales + (jb * 8 + pg) * 2048, &tm_scales, &ctl->sc_full,
-                            p.ks_x0 + 128 * jb, slot[pg], blk[pg]);
+              tma_load_3d(smem + SL.sc + pg * 16 * p.sc_pitch, &tm_sc, &ctl->sc_full, p.sc_x0 / 8, slot[pg], blk[pg]);
           }
         }
-        const int ab_row0 = (b * p.group + j) * p.k_width;
-        for (int c = 0; ok && c < NC; ++c, ++ab_it, ++code_it) {
+        // this CTA's half of each AB chunk (lanes [64 rank, 64 rank + 64) of the chunk):
+        // 16 KB image blocks, 8 rows of 2 KB each
+        const int ab_row0 = ((b * p.group + j) * NC * 2 + (int)rank) * 8;
+        for (int c = 0; ok && c < NC; ++c, ++ab_it) {
+          if (c % C::kChunksPerWin == 0) {
+            // next code window of this CTA's tokens: one box of 16 rows per page
+            const int w = c / C::kChunksPerWin;
+            const bool tail = w == p.n_wins - 1;
+            const int pitch = tail ? p.tail_pitch : p.code_pitch;
+            const int sc = code_it % kCodeSlots;
+            if (!mbar_wait(&ctl->code_empty[sc], ((code_it / kCodeSlots) & 1) ^ 1, abort_flag, p.status)) {
+              ok = 0;
+              break;
+            }
+            uint8_t* cds = smem + SL.codes + sc * SL.code_slot;
+            mbar_arrive_expect_tx(&ctl->code_full[sc], kTile * pitch);
+#pragma unroll
+            for (int pg = 0; pg < 8; ++pg)
+              tma_load_3d(cds + pg * 16 * pitch, tail ? &tm_tail : &tm_code, &ctl->code_full[sc], w * win_u64,
+                          slot[pg], blk[pg]);
+            ++code_it;
+          }
           const int sa = ab_it % kAbSlots;
           if (!mbar_wait(&ctl->ab_empty[sa], ((ab_it / kAbSlots) & 1) ^ 1, abort_flag, p.status)) {
             ok = 0;
             break;
           }
-          uint8_t* abs = smem + LY::kOffAb + sa * kAbBytes;
-          mbar_arrive_expect_tx(&ctl->ab_full[sa], kAbBytes);
-          tma_load_2d(abs, &tm_ab, &ctl->ab_full[sa], 0, ab_row0 + c * kChunk);
-          tma_load_2d(abs + kAbBytes / 2, &tm_ab, &ctl->ab_full[sa], 64, ab_row0 + c * kChunk);
-          const int sc = code_it % LY::kCodeSlots;
-          if (!mbar_wait(&ctl->code_empty[sc], ((code_it / LY::kCodeSlots) & 1) ^ 1, abort_flag, p.status)) {
-            ok = 0;
-            break;
-          }
-          uint8_t* cds = smem + LY::kOffCodes + sc * LY::kCodeBytes;
-          mbar_arrive_expect_tx(&ctl->code_full[sc], LY::kCodeBytes);
-#pragma unroll
-          for (int pg = 0; pg < 8; ++pg)
-#pragma unroll
-            for (int i = 0; i < LY::kCodeBoxes; ++i) {
-              const int x = QUANT ? c * 64 : c * kChunk + 64 * i;
-              tma_load_3d(cds + (i * 8 + pg) * LY::kCodeBoxBytes, &tm_codes, &ctl->code_full[sc], x, slot[pg],
-                          blk[pg]);
-            }
+          uint8_t* abs = smem + SL.ab + sa * kAbBytes;
+          const uint32_t full_l = leader_addr(&ctl->ab_full[sa]);
+          if (rank == 0) mbar_arrive_expect_tx(&ctl->ab_full[sa], 2 * kAbBytes);
+          tma_load_2d_pair(abs, &tm_ab, full_l, 0, ab_row0 + c * 16);
         }
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
     }
+    // Drain: wait for the MMA completions still to be multicast into this CTA's
+    // empty barriers (the last AB slots and the last rotary rows), so none lands
+    // after the CTA has left.
+    if (lane == 0 && !*abort_flag) {
+      for (int k = 0; k < kAbSlots; ++k) {
+        const uint32_t it = ab_it + k;
+        if (!mbar_wait(&ctl->ab_empty[it % kAbSlots], ((it / kAbSlots) & 1) ^ 1, abort_flag, p.status)) break;
+      }
+      mbar_wait(&ctl->cs_empty, (item_cnt & 1) ^ 1, abort_flag, p.status);
+    }
   } else if (warp == 1) {
-    // ================= MMA issuer =================
-    if (lane == 0) {
-      const uint32_t idesc = instr_desc_f16(/*f16*/ 0, 0, 0, kTile, kChunk);
+    // ================= MMA issuer (CTA 0 of the pair) =================
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = instr_desc_f16(/*f16*/ 0, 0, 0, kPairTokens, kChunk);
       uint32_t ab_it = 0, tb = 0, item_cnt = 0;
-      const uint32_t cs_addr = smem_u32(smem + LY::kOffCs);
-      for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x, ++item_cnt) {
+      const uint32_t cs_addr = smem_u32(smem + SL.cs);
+      for (int item = pair; item < total_items && !*abort_flag; item += n_pairs, ++item_cnt) {
         if (!mbar_wait(&ctl->cs_full, item_cnt & 1, abort_flag, p.status)) break;
         tc_fence_after();
         for (int c = 0; c < NC; ++c, ++ab_it, ++tb) {
@@ -289,31 +335,30 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
           if (!mbar_wait(&ctl->ab_full[sa], (ab_it / kAbSlots) & 1, abort_flag, p.status)) break;
           if (!mbar_wait(&ctl->tempty[buf], ((tb / kTmemBufs) & 1) ^ 1, abort_flag, p.status)) break;
           tc_fence_after();
-          const uint32_t ab_addr = smem_u32(smem + LY::kOffAb + sa * kAbBytes);
+          const uint32_t ab_addr = smem_u32(smem + SL.ab + sa * kAbBytes);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t da = smem_desc(cs_addr + (kk >> 2) * (kCsBytes / 2) + (kk & 3) * 32, 16, 1024,
                                           kSwizzle128B);
             const uint64_t db = smem_desc(ab_addr + (kk >> 2) * (kAbBytes / 2) + (kk & 3) * 32, 16, 1024,
                                           kSwizzle128B);
-            umma_f16(tmem + buf * kChunk, da, db, idesc, kk > 0);
+            umma_f16_pair(tmem + buf * kChunk, da, db, idesc, kk > 0);
           }
-          umma_commit(&ctl->ab_empty[sa]);
-          umma_commit(&ctl->tfull[buf]);
+          umma_commit_pair(&ctl->ab_empty[sa]);
+          umma_commit_pair(&ctl->tfull[buf]);
         }
-        umma_commit(&ctl->cs_empty);
+        umma_commit_pair(&ctl->cs_empty);
       }
     }
   } else {
-    // ================= epilogue (warps 2 .. 2 + kEpiWarps) =================
-    // Thread = (token row of the tile, column group of the chunk): warp w may only
-    // read TMEM lanes 32 (w % 4) .. +32, so the warps cover the 4 lane quarters x
-    // kGroups column groups of kSub x 32 columns.
-    const int ew = warp - 2;              // 0..kEpiWarps-1
+    // ================= epilogue (warps 2-17, both CTAs) =================
+    // Thread = (token row of this CTA's tile, 32-lane group g of the chunk): warp w
+    // may only read TMEM lanes 32 (w % 4) .. +32, so the 16 warps cover the 4 lane
+    // quarters x 4 groups.
+    const int ew = warp - 2;              // 0..15
     const int q = warp & 3;               // TMEM lane quarter this warp may access
-    const int gq = ew >> 2;               // column group: chunk columns [32 kSub gq, 32 kSub (gq + 1))
+    const int g = ew >> 2;                // 32-lane group: chunk columns [32 g, 32 g + 32)
     const int row = q * 32 + lane;        // token within the tile
-    const int pg = row >> 4, sl = row & 15;
     uint32_t code_it = 0, tb = 0, item_cnt = 0, epi_phase = 0;
     // Bounded barrier among the epilogue threads (a plain bar.sync could wait
     // forever if another epilogue warp left on a timed-out pipeline wait).
@@ -321,12 +366,13 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       mbar_arrive(&ctl->epi);
       return mbar_wait(&ctl->epi, (epi_phase++) & 1, abort_flag, p.status);
     };
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++item_cnt) {
+    const uint32_t tempty_l = leader_addr(&ctl->tempty[0]);
+    for (int item = pair; item < total_items; item += n_pairs, ++item_cnt) {
       if (*abort_flag) break;
       const int b = find_seq(prefix, p.n, item);
       const int rem = item - prefix[b];
       const int j = rem % p.group;
-      const int tile = rem / p.group;
+      const int tile = (rem / p.group) * 2 + (int)rank;   // this CTA's 128-token tile
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int t0 = tile * kTile;
       if (QUANT && !mbar_wait(&ctl->sc_full, item_cnt & 1, abort_flag, p.status)) break;
@@ -343,11 +389,8 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         float v;
         if (QUANT) {
           // (outlier, inlier) bf16 scales of head cur_h for this token
-          const int off = p.ks_off + 4 * cur_h - p.ks_x0;
-          const int jb = off >> 7, within = off & 127;
-          const uint8_t* sb = smem + LY::kOffScales + (jb * 8 + pg) * 2048 + sl * 128;
-          const uint32_t sw =
-              *reinterpret_cast<const uint32_t*>(sb + ((((within >> 4) ^ (sl & 7)) << 4) | (within & 15)));
+          const uint32_t sw = *reinterpret_cast<const uint32_t*>(smem + SL.sc + row * p.sc_pitch + p.ks_off +
+                                                                 4 * cur_h - p.sc_x0);
           const float so = __uint_as_float(sw << 16), si = __uint_as_float(sw & 0xFFFF0000u);
           const float out = (ao[0].x + ao[0].y) + (ao[1].x + ao[1].y);
           v = si * all + (so - si) * out;
@@ -360,46 +403,44 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         ao[0] = ao[1] = make_float2(0.f, 0.f);
       };
       bool ok = true;
-      for (int c = 0; c < NC; ++c, ++code_it, ++tb) {
-        const int sc = code_it % LY::kCodeSlots;
+      int sc = 0;
+      const uint8_t* crow = nullptr;   // this token's row of the current code window
+      for (int c = 0; c < NC; ++c, ++tb) {
         const int buf = tb % kTmemBufs;
-        if (!mbar_wait(&ctl->tfull[buf], (tb / kTmemBufs) & 1, abort_flag, p.status) ||
-            !mbar_wait(&ctl->code_full[sc], (code_it / LY::kCodeSlots) & 1, abort_flag, p.status)) {
+        const int cw = c % C::kChunksPerWin;
+        if (cw == 0) {
+          sc = code_it % kCodeSlots;
+          const int pitch = (c / C::kChunksPerWin == p.n_wins - 1) ? p.tail_pitch : p.code_pitch;
+          crow = smem + SL.codes + sc * SL.code_slot + row * pitch;
+          if (!mbar_wait(&ctl->code_full[sc], (code_it / kCodeSlots) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!mbar_wait(&ctl->tfull[buf], (tb / kTmemBufs) & 1, abort_flag, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t zr[EP::kSub][32];
-        const int nsub = min(EP::kSub, max(0, (NT * 16 - c * kChunk - 32 * EP::kSub * gq + 31) / 32));   // warp-uniform
-#pragma unroll
-        for (int sb = 0; sb < EP::kSub; ++sb)
-          if (sb < nsub)
-            tmem_ld32_issue(tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk + 32 * (EP::kSub * gq + sb), zr[sb]);
-#pragma unroll
-        for (int sb = 0; sb < EP::kSub; ++sb) {
-          if (sb >= nsub) break;
-          const int g = EP::kSub * gq + sb;     // 32-lane group of the chunk
-          const uint8_t* codes = smem + LY::kOffCodes + sc * LY::kCodeBytes;
-          // this token's codes of the group's 32 lanes
+        if (NT * 16 > c * kChunk + 32 * g) {   // this group holds real lanes (warp-uniform)
+          uint32_t z[32];
+          tmem_ld32_issue(tmem + ((uint32_t)(q * 32) << 16) + buf * kChunk + 32 * g, z);
+          // this token's codes of the group's 32 lanes, read while the TMEM load is in flight
+          const int lane_in_win = cw * kChunk + 32 * g;
           constexpr int kWords = QUANT ? 4 : 16;
           uint32_t w[kWords];
           if (QUANT) {
-            const uint8_t* box = codes + pg * LY::kCodeBoxBytes;
-            const int phys = g ^ ((sl >> 1) & 3);     // 64-byte swizzle
-            const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 64 + phys * 16);
+            const uint4 u = *reinterpret_cast<const uint4*>(crow + lane_in_win / 2);
             w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
           } else {
-            const uint8_t* box = codes + ((g >> 1) * 8 + pg) * LY::kCodeBoxBytes;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
-              const int phys = ((g & 1) * 4 + v) ^ (sl & 7);   // 128-byte swizzle
-              const uint4 u = *reinterpret_cast<const uint4*>(box + sl * 128 + phys * 16);
+              const uint4 u = *reinterpret_cast<const uint4*>(crow + lane_in_win * 2 + 16 * v);
               w[4 * v] = u.x; w[4 * v + 1] = u.y; w[4 * v + 2] = u.z; w[4 * v + 3] = u.w;
             }
           }
-          const int2 m2 = reinterpret_cast<const int2*>(tiles)[c * 4 + g];   // metadata of the 2 lane tiles
-          tmem_wait(zr[sb]);   // the first waits for all loads; each names its own registers
-          const uint32_t* z = zr[sb];
+          const int2 m2 = reinterpret_cast<const int2*>(tiles)[c * kGroups + g];   // the 2 lane tiles
+          tmem_wait(z);
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int meta = hh == 0 ? m2.x : m2.y;
@@ -458,9 +499,10 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&ctl->tempty[buf]);
-          mbar_arrive(&ctl->code_empty[sc]);
+          mbar_arrive_cluster(tempty_l + 8u * buf);   // the MMA issuer's barrier, in CTA 0
+          if (cw == C::kChunksPerWin - 1 || c == NC - 1) mbar_arrive(&ctl->code_empty[sc]);
         }
+        if (cw == C::kChunksPerWin - 1 || c == NC - 1) ++code_it;
       }
       if (cur_h >= 0) flush();
       if (QUANT) {
@@ -468,51 +510,40 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         if (lane == 0) mbar_arrive(&ctl->sc_empty);
       }
       if (!ok || !epi_sync()) break;
-      // ---- per-head tile softmax statistics: warp ew owns kTokPerWarp tokens ----
-      constexpr int kTokPerWarp = EP::kTokPerWarp;
-      for (int h = lane; h < H; h += 32) {
-        float m = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kTokPerWarp; ++i) {
-          const int t = kTokPerWarp * ew + i;
-          if (t0 + t < L) m = fmaxf(m, logits[h * (kTile + 1) + t]);
-        }
-        red_m[ew * H + h] = m;
-      }
-      if (!epi_sync()) break;
-      for (int h = lane; h < H; h += 32) {
-        float m = red_m[h];
-        for (int w2 = 1; w2 < kEpiWarps; ++w2) m = fmaxf(m, red_m[w2 * H + h]);
-        const int hq = h * p.group + j;
-        float ssum = 0.f;
-        __align__(16) __half ev[kTokPerWarp];
-#pragma unroll
-        for (int i = 0; i < kTokPerWarp; ++i) {
-          const int t = kTokPerWarp * ew + i;
-          float v = 0.f;
-          if (t0 + t < L) v = __expf(logits[h * (kTile + 1) + t] - m);
-          ssum += v;
-          ev[i] = __float2half_rn(v);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + kTokPerWarp * ew);
-#pragma unroll
-        for (int i = 0; i < kTokPerWarp / 8; ++i) dst[i] = reinterpret_cast<const uint4*>(ev)[i];
-        red_l[ew * H + h] = ssum;
-      }
-      if (!epi_sync()) break;
-      if (ew == 0) {
+      if (t0 < L) {
+        // ---- per-head tile max and e16 = exp(logit - max): warp ew owns 8 tokens ----
         for (int h = lane; h < H; h += 32) {
-          float m = red_m[h], l = red_l[h];
-          for (int w2 = 1; w2 < kEpiWarps; ++w2) {
-            m = fmaxf(m, red_m[w2 * H + h]);
-            l += red_l[w2 * H + h];
+          float m = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < kTokPerWarp; ++i) {
+            const int t = kTokPerWarp * ew + i;
+            if (t0 + t < L) m = fmaxf(m, logits[h * (kTile + 1) + t]);
           }
-          const int hq = h * p.group + j;
-          const int64_t mi = ((int64_t)b * p.num_heads + hq) * p.n_tiles + tile;
-          p.m_tile[mi] = m;
-          (void)l;
-          atomic_max_f32(p.m_seq + (int64_t)b * p.num_heads + hq, m);
+          red_m[ew * H + h] = m;
         }
+        if (!epi_sync()) break;
+        for (int h = lane; h < H; h += 32) {
+          float m = red_m[h];
+          for (int w2 = 1; w2 < kEpiWarps; ++w2) m = fmaxf(m, red_m[w2 * H + h]);
+          const int hq = h * p.group + j;
+          __align__(16) __half ev[kTokPerWarp];
+#pragma unroll
+          for (int i = 0; i < kTokPerWarp; ++i) {
+            const int t = kTokPerWarp * ew + i;
+            float v = 0.f;
+            if (t0 + t < L) v = __expf(logits[h * (kTile + 1) + t] - m);
+            ev[i] = __float2half_rn(v);
+          }
+          uint4* dst =
+              reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + kTokPerWarp * ew);
+#pragma unroll
+          for (int i = 0; i < kTokPerWarp / 8; ++i) dst[i] = reinterpret_cast<const uint4*>(ev)[i];
+          if (ew == 0) {
+            p.m_tile[((int64_t)b * p.num_heads + hq) * p.n_tiles + tile] = m;
+            atomic_max_f32(p.m_seq + (int64_t)b * p.num_heads + hq, m);
+          }
+        }
+        if (!epi_sync()) break;
       }
       // clear the logits for the next tile's atomic flushes
       for (int i = threadIdx.x - 64; i < H * (kTile + 1); i += 32 * kEpiWarps) logits[i] = 0.f;
@@ -520,32 +551,65 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     }
   }
 
-  // ---- teardown ----
+  // ---- teardown: no pair MMA, remote arrive or commit may target a CTA that left ----
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemBufs * kChunk);
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
-int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_codes,
-                  const CUtensorMap& tm_scales, const ScoresParams& p, int num_sms, cudaStream_t stream) {
-  const size_t smem = scores_smem_bytes(quant, p.num_kv_heads, p.n, p.k_width, quant ? p.ks_boxes : 0);
-  if (smem > 227 * 1024) return STARKV_EINVAL;
-  const bool f16 = p.cache_dtype == STARKV_F16;
-  const void* fn = quant ? (const void*)scores_kernel<true, false>
-                         : (f16 ? (const void*)scores_kernel<false, true> : (const void*)scores_kernel<false, false>);
+namespace {
+
+template <bool QUANT, bool F16>
+int launch_pairs(const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
+                 const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
+                 size_t smem, cudaStream_t stream) {
+  auto fn = scores_kernel<QUANT, F16>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return STARKV_ECUDA;
-  const int grid = num_sms;
-  if (quant)
-    scores_kernel<true, false><<<grid, Epi<true>::kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
-  else if (f16)
-    scores_kernel<false, true><<<grid, Epi<false>::kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
-  else
-    scores_kernel<false, false><<<grid, Epi<false>::kThreads, smem, stream>>>(tm_cs, tm_ab, tm_codes, tm_scales, p);
-  return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // persistent: as many pairs as can be resident at once (SMs that cannot be
+  // paired inside a GPC stay idle rather than run a second wave)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int max_pairs[64][2] = {};
+  int& mp = max_pairs[dev & 63][QUANT ? 1 : 0];
+  if (mp == 0) {
+    cfg.gridDim = dim3(num_sms & ~1);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, (const void*)fn, &cfg) != cudaSuccess || clusters <= 0)
+      clusters = num_sms / 2;
+    mp = clusters < num_sms / 2 ? clusters : num_sms / 2;
+  }
+  cfg.gridDim = dim3(2 * mp);
+  if (cudaLaunchKernelEx(&cfg, fn, tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p) != cudaSuccess) return STARKV_ECUDA;
+  return STARKV_OK;
+}
+
+}  // namespace
+
+int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
+                  const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
+                  cudaStream_t stream) {
+  const size_t smem = scores_smem_bytes(quant, p.num_kv_heads, p.n, p.k_width, p.code_pitch, p.sc_pitch);
+  if (smem > 227 * 1024) return STARKV_EINVAL;
+  if (quant) return launch_pairs<true, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
+  if (p.cache_dtype == STARKV_F16)
+    return launch_pairs<false, true>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
+  return launch_pairs<false, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
 }
 
 }  // namespace starkv

@@ -38,7 +38,10 @@ struct ScoresParams {
   const int32_t* tile_head;
   const int32_t* tile_nout;
   const int32_t* tile_last;
-  int ks_off, ks_x0, ks_boxes;     // 3.2-bit: K scales at ks_off; boxes of 128 B from ks_x0
+  int ks_off;                      // 3.2-bit: byte offset of the K scales in a row
+  int code_pitch, tail_pitch;      // staged row pitch of a full / the last code window (bytes)
+  int n_wins;                      // code windows per row
+  int sc_pitch, sc_x0;             // 3.2-bit: staged scale window (pitch, 16-aligned byte start)
   __half* e16;
   float* m_tile;
   float* m_seq;
@@ -87,22 +90,28 @@ struct FoldParams {
   const int32_t* k_head_offsets;
   int n, num_heads, num_kv_heads, group, k_width, head_dim;
   float scale;
-  __half* ab;                      // [n, group, W, 128]
+  __half* ab;                      // [n, group, W, 128], or the MMA image below when ab_image
+  int ab_image;                    // 1: per (b, j, 128-lane chunk c, 64-lane half r) a 16 KB block
+                                   //    [k half][64 lanes][128 B], 16-byte units XOR-swizzled by lane & 7
   // rotary table -> f16 copy
   const void* cs; int64_t cs_s0, cs_s1; int cs_dtype; int cs_rows;
-  __half* cs16; int l_pad, max_seq_len;
+  __half* cs16; int l_pad, max_seq_len;   // per 128-token tile a 32 KB block [k half][128 rows][128 B],
+                                          // 16-byte units XOR-swizzled by row & 7
   // per-call initialisation
   float* m_seq; float* l_seq; int m_count;
   float* pv; int64_t pv_count;
   int32_t* status;
 };
 
-size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int ks_boxes);
+size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch);
+int code_pitch_bytes(int bytes);
+int scores_window_bytes(bool quant);
 size_t pv_smem_bytes(bool quant, const PvParams& p);
 
 int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream);
-int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_codes,
-                  const CUtensorMap& tm_scales, const ScoresParams& p, int num_sms, cudaStream_t stream);
+int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
+                  const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
+                  cudaStream_t stream);
 int launch_pv(bool quant, const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms,
               cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
