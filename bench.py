@@ -10,10 +10,14 @@ reported under "q32". Inputs are seeded synthetic tensors with the configs'
 shapes and distributions (starkv_b200.workload); every step reads a >2 GB cache,
 far larger than the 126 MB L2, so no flush is needed between steps.
 
-N > 1 (torchrun): heads are sharded tensor-parallel across ranks, balanced by K
-rank (LPT), V codes replicated (the shared latent is read by every head); the
-step time is the max over ranks and `value` counts the batch's decode tokens
-once (strong scaling: the total work is fixed).
+N > 1 (torchrun), --parallel context (default): every rank decodes all heads over
+its share of each sequence's 256-token tiles, and the partial results are combined
+exactly with two small NCCL all-reduces inside the step (starkv_b200.context_parallel);
+each GPU reads 1/N of the K and V codes. --parallel heads: heads sharded
+tensor-parallel (LPT on K width), V codes replicated on every rank (the shared
+latent is read by every head), no collective. Either way the step time is the max
+over ranks and `value` counts the batch's decode tokens once (strong scaling: the
+total work is fixed).
 
 --impl reference: the reference algorithm's CPU restatement (oracle/), timed on
 this host's cores on a bounded sample of the same workload.
@@ -122,18 +126,20 @@ def shard_layer_spec(ranks, world, rank):
     return lpt_shard(ranks, world)[rank]
 
 
-def build_layer(quant: bool, world: int, rank: int, device, batch=None, context=None):
+def build_layer(quant: bool, world: int, rank: int, device, batch=None, context=None, parallel="context"):
     from starkv_b200.workload import make_layer, sample_ranks
     n, L = (64, 16384) if quant else (64, 8192)
     n, L = batch or n, context or L
     ranks, rv = sample_ranks(32, 0)
-    heads = list(range(32)) if world == 1 else shard_layer_spec(ranks, world, rank)
+    # context split: every rank holds the whole layer (all heads) and decodes its
+    # share of each sequence; head split: each rank holds its heads (LPT)
+    heads = list(range(32)) if world == 1 or parallel == "context" else shard_layer_spec(ranks, world, rank)
     local = [ranks[h] for h in heads]
     layer = make_layer([L] * n, num_heads=len(local), quant=quant, seed=0, device=device, ranks=local, v_rank=rv)
     return layer, heads
 
 
-def run_step_fns(layer, device):
+def run_step_fns(layer, device, cp=None):
     import torch
     from starkv_b200.kernels import paged_quant as pq
     from starkv_b200.kernels.paged_decode import paged_starkv_decode, write_kv_bf16
@@ -150,7 +156,11 @@ def run_step_fns(layer, device):
     slots = (layer.block_table[torch.arange(n, device=device), pos // 16].long() * 16 + pos % 16)
     H = layer.num_heads
     ws = workspace.reserve(device, n, H, len(layer.ranks), layer.k_width, layer.v_rank, layer.max_seq_len)
-    out = torch.empty(n, H, 128, dtype=torch.bfloat16, device=device)
+    out = torch.empty(n, H, 128, dtype=torch.float32 if cp else torch.bfloat16, device=device)
+    # context split: the new token of every sequence lies in the last rank's share
+    writes = cp is None or cp[0] == cp[1] - 1
+    if cp is not None:
+        from starkv_b200.context_parallel import combine
 
     def step(q=None, kn=None, vn=None, bt=None, sl=None):
         q = layer.query if q is None else q
@@ -159,23 +169,28 @@ def run_step_fns(layer, device):
         bt = layer.block_table if bt is None else bt
         sl = layer.seq_lens if sl is None else sl
         if layer.quant:
-            pq.pack_kv(kn, vn, layer.kv_cache, slots, layer.row, layer.k_ranks, layer.k_head_offsets, layer.k_nouts)
-            return pq.paged_quant_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.row, layer.k_up,
-                                         layer.head_of_lane, layer.k_tiles, layer.v_up_by_q, layer.cos_sin_cache,
-                                         layer.scale, out=out, ws=ws)
-        write_kv_bf16(kn, vn, layer.kv_cache, slots)
-        return paged_starkv_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.k_up, layer.k_ranks,
-                                   layer.k_head_offsets, layer.k_width, layer.v_up_by_q, layer.cos_sin_cache,
-                                   layer.scale, out=out, ws=ws)
+            if writes:
+                pq.pack_kv(kn, vn, layer.kv_cache, slots, layer.row, layer.k_ranks, layer.k_head_offsets,
+                           layer.k_nouts)
+            r = pq.paged_quant_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.row, layer.k_up,
+                                      layer.head_of_lane, layer.k_tiles, layer.v_up_by_q, layer.cos_sin_cache,
+                                      layer.scale, out=out, ws=ws, context=cp)
+        else:
+            if writes:
+                write_kv_bf16(kn, vn, layer.kv_cache, slots)
+            r = paged_starkv_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.k_up, layer.k_ranks,
+                                    layer.k_head_offsets, layer.k_width, layer.v_up_by_q, layer.cos_sin_cache,
+                                    layer.scale, out=out, ws=ws, context=cp)
+        return combine(*r) if cp is not None else r
     return step, (k_new, v_new)
 
 
-def measure(layer, device, steps, warmup, dist_on):
+def measure(layer, device, steps, warmup, dist_on, cp=None):
     import ctypes as C
     import torch
     import torch.distributed as dist
     from starkv_b200 import _lib
-    step, (k_new, v_new) = run_step_fns(layer, device)
+    step, (k_new, v_new) = run_step_fns(layer, device, cp)
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
@@ -239,9 +254,21 @@ def measure(layer, device, steps, warmup, dist_on):
     return ms, per_kernel, clocks, e2e_ms, h2d, d2h
 
 
-def roofline_for(layer, per_kernel, hbm_peak):
+def rank_tokens(layer, cp):
+    """Tokens this rank decodes: all, or its share of each sequence's 256-token tiles."""
+    if cp is None:
+        return layer.kv_tokens()
+    r, w = cp
+    tot = 0
+    for L in layer.seq_lens_host:
+        T = -(-L // 256)
+        tot += max(0, min(256 * (T * (r + 1) // w), L) - 256 * (T * r // w))
+    return tot
+
+
+def roofline_for(layer, per_kernel, hbm_peak, cp=None):
     """Dominant kernel's algorithmic bytes per launch / its event-timed duration."""
-    T = layer.kv_tokens()
+    T = rank_tokens(layer, cp)
     names = ["fold", "scores", "pv", "lift"]
     k = max(range(4), key=lambda i: per_kernel[i])
     if layer.quant:
@@ -312,11 +339,12 @@ def ours(args):
     res = {}
     cases = {"c2": (False,), "c3": (True,), "both": (False, True)}[args.case]
     for quant in cases:
-        layer, heads = build_layer(quant, world, rank, device, args.batch, args.context)
-        ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on)
+        layer, heads = build_layer(quant, world, rank, device, args.batch, args.context, args.parallel)
+        cp = (rank, world) if dist_on and args.parallel == "context" else None
+        ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on, cp)
         res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
                           d2h=d2h, alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
-                          roof=roofline_for(layer, per_kernel, hbm_peak))
+                          roof=roofline_for(layer, per_kernel, hbm_peak, cp))
         del layer
         torch.cuda.empty_cache()
     if rank == 0 and args.case != "both":
@@ -337,25 +365,27 @@ def ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(b["ms"], 4), "us_per_layer": round(b["ms"] * 1e3, 1),
             "hbm_gbs": round(b["alg"] / (b["ms"] * 1e-3) / 1e9, 1),
-            "hbm_frac_step": round(b["alg"] / (b["ms"] * 1e-3) / 1e9 / hbm_peak, 4),
+            "hbm_frac_step": round(b["alg"] / (b["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config shapes)",
             "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
                                    "32 heads x 128, page 16, cache write + decode per step",
-                       "batch": 64, "context": 8192, "heads_per_gpu": 32 // world,
-                       "parallelism": f"tp{world} (heads)" if world > 1 else "single",
+                       "batch": 64, "context": 8192,
+                       "heads_per_gpu": 32 if world == 1 or args.parallel == "context" else 32 // world,
+                       "parallelism": ("single" if world == 1 else f"cp{world} (context split, all heads per GPU)"
+                                       if args.parallel == "context" else f"tp{world} (heads)"),
                        "l2": "inputs (2.9 GB cache) larger than L2; no flush"},
             "roofline": dict(b["roof"], peak_kind=peak_kind),
             "e2e": {"value": round(n / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": b["h2d"], "d2h_bytes_per_step": b["d2h"],
                     "ms_per_step": round(b["e2e_ms"], 4)},
-            "gpu_launches": 5 * args.steps,
+            "gpu_launches": (5 if world == 1 or args.parallel != "context" or rank == world - 1 else 4) * args.steps,
             "clocks": b["clocks"],
             "q32": {"workload": "config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
                     "value": round(q["layer"].n / (q["ms"] * 1e-3), 1), "unit": UNIT, "ms_per_step": round(q["ms"], 4),
                     "us_per_layer": round(q["ms"] * 1e3, 1),
                     "hbm_gbs": round(q["alg"] / (q["ms"] * 1e-3) / 1e9, 1),
-                    "hbm_frac_step": round(q["alg"] / (q["ms"] * 1e-3) / 1e9 / hbm_peak, 4),
+                    "hbm_frac_step": round(q["alg"] / (q["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
                     "tflops": round(q["flops"] / (q["ms"] * 1e-3) / 1e12, 1),
                     "roofline": dict(q["roof"], peak_kind=peak_kind),
                     "e2e_ms_per_step": round(q["e2e_ms"], 4), "clocks": q["clocks"]},
@@ -398,6 +428,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default="both", choices=["both", "c2", "c3"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
+    ap.add_argument("--parallel", default="context", choices=["context", "heads"],
+                    help="N > 1: split every sequence's tiles over the GPUs (all heads each), or shard heads")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling small cases)")
     ap.add_argument("--context", type=int, default=None, help="override the context (profiling small cases)")
     a = ap.parse_args()

@@ -129,6 +129,27 @@ STARKV_API int starkv_paged_decode_q32(const StarKVDecodeArgs* args, void* works
                             void* stream);
 
 /*
+ * Context-parallel share of the two decodes above: the next step after
+ * head sharding for multi-GPU decode (the reference has no multi-GPU path;
+ * model.py:32-33 rejects tensor parallelism). Rank cp_rank of cp_world decodes,
+ * for every head, its contiguous share of each sequence's 256-token tiles
+ * (tiles [T*r/w, T*(r+1)/w) of T = ceil(seq_len/256)) and returns
+ *   out   f32 [n, num_heads, 128] (args->out, out_dtype STARKV_F32):
+ *         sum_t exp(logit_t - m) V_t . v_up_by_q, unnormalised;
+ *   m_out f32 [n, num_heads]: that max m of the rank's logits (-inf if the rank
+ *         holds no token of the sequence); l_out: sum_t exp(logit_t - m).
+ * Ranks combine as out = sum_r exp(m_r - M) out_r / sum_r exp(m_r - M) l_r with
+ * M = max_r m_r (starkv_b200.context_parallel). cp_world = 1 gives the whole
+ * sequence. Errors as for the full decode.
+ */
+STARKV_API int starkv_paged_decode_bf16_partial(const StarKVDecodeArgs* args, int32_t cp_rank, int32_t cp_world,
+                                                float* m_out, float* l_out, void* workspace, size_t workspace_bytes,
+                                                void* stream);
+STARKV_API int starkv_paged_decode_q32_partial(const StarKVDecodeArgs* args, int32_t cp_rank, int32_t cp_world,
+                                               float* m_out, float* l_out, void* workspace, size_t workspace_bytes,
+                                               void* stream);
+
+/*
  * paged_quant.py:241-255 (fold_q): q [n, H, 128] (RoPE applied), k_up [W, 128],
  * head_of_lane [W] -> ab [n, W, 128] f16 (contiguous), the logit scale folded in:
  *   A[r,i] = (q_i U[r,i] + q_{i+64} U[r,i+64]) * scale

@@ -106,8 +106,17 @@ Workspace workspace_layout(int n, int num_heads, int num_kv_heads, int k_width, 
   return w;
 }
 
-static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_bytes, cudaStream_t stream, bool quant) {
+// cp_world > 1 (or m_out set): context-parallel partial decode of this rank's share of
+// every sequence; out is then f32 and unnormalised (sum_t p_t V_t . v_up with p
+// relative to the rank's own per-head max), and the max / softmax denominator go to
+// m_out / l_out [n, num_heads] f32.
+static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_bytes, cudaStream_t stream, bool quant,
+                       int cp_rank = 0, int cp_world = 1, float* m_out = nullptr, float* l_out = nullptr) {
   if (!a) return STARKV_EINVAL;
+  if (cp_world < 1 || cp_rank < 0 || cp_rank >= cp_world) return STARKV_EINVAL;
+  const bool partial = m_out != nullptr || l_out != nullptr;
+  if (partial && (!m_out || !l_out || a->out_dtype != STARKV_F32)) return STARKV_EINVAL;
+  if (cp_world > 1 && !partial) return STARKV_EINVAL;   // a share of a sequence is only a partial result
   DeviceInfo dev;
   int st = device_info(dev);
   if (st) return st;
@@ -255,6 +264,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   sp.sc_pitch = sc_pitch; sp.sc_x0 = sc_x0;
   sp.e16 = e16; sp.m_tile = m_tile; sp.m_seq = m_seq;
   sp.l_pad = ws.l_pad; sp.n_tiles = ws.n_tiles; sp.status = status;
+  sp.cp_rank = cp_rank; sp.cp_world = cp_world;
   if ((st = launch_scores(quant, tm_cs, tm_ab, tm_code, tm_tail, tm_sc, sp, dev.sms, stream))) return st;
   if (pev) cudaEventRecord(pev[2], stream);
 
@@ -292,6 +302,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   pp.mt_per_range = (pp.n_mtiles + pp.n_ranges - 1) / pp.n_ranges;   // balance the ranges
   pp.e16 = e16; pp.m_tile = m_tile; pp.m_seq = m_seq; pp.l_seq = l_seq; pp.pv = pv; pp.pv_stride = ws.pv_stride;
   pp.l_pad = ws.l_pad; pp.n_tiles = ws.n_tiles; pp.status = status;
+  pp.cp_rank = cp_rank; pp.cp_world = cp_world;
   CUtensorMap tm_e;
   {
     const uint64_t dims[2] = {(uint64_t)ws.l_pad, (uint64_t)a->n * a->num_heads};
@@ -305,7 +316,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
 
   // ---- lift ----
   LiftParams lp{};
-  lp.pv = pv; lp.pv_stride = ws.pv_stride; lp.l_seq = l_seq;
+  lp.pv = pv; lp.pv_stride = ws.pv_stride; lp.l_seq = partial ? nullptr : l_seq;   // partial: no normalisation
   lp.v_up = a->v_up_by_q; lp.vu_s0 = a->v_up_stride[0]; lp.vu_s1 = a->v_up_stride[1]; lp.vu_s2 = a->v_up_stride[2];
   lp.v_up_dtype = a->v_up_dtype;
   lp.out = a->out; lp.o_s0 = a->out_stride[0]; lp.o_s1 = a->out_stride[1]; lp.o_s2 = a->out_stride[2];
@@ -313,6 +324,12 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   lp.n = a->n; lp.num_heads = a->num_heads; lp.v_rank = a->v_rank;
   lp.head_dim = a->head_dim;
   st = launch_lift(lp, stream);
+  if (st == STARKV_OK && partial) {
+    const size_t bytes = (size_t)a->n * a->num_heads * sizeof(float);
+    if (cudaMemcpyAsync(m_out, m_seq, bytes, cudaMemcpyDeviceToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync(l_out, l_seq, bytes, cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+      st = STARKV_ECUDA;
+  }
   if (pev) cudaEventRecord(pev[4], stream);
   return st;
 }
@@ -333,6 +350,20 @@ int starkv_paged_decode_bf16(const StarKVDecodeArgs* args, void* workspace, size
 
 int starkv_paged_decode_q32(const StarKVDecodeArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
   return starkv::decode_impl(args, workspace, workspace_bytes, (cudaStream_t)stream, true);
+}
+
+int starkv_paged_decode_bf16_partial(const StarKVDecodeArgs* args, int32_t cp_rank, int32_t cp_world, float* m_out,
+                                     float* l_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m_out || !l_out) return STARKV_EINVAL;
+  return starkv::decode_impl(args, workspace, workspace_bytes, (cudaStream_t)stream, false, cp_rank, cp_world, m_out,
+                             l_out);
+}
+
+int starkv_paged_decode_q32_partial(const StarKVDecodeArgs* args, int32_t cp_rank, int32_t cp_world, float* m_out,
+                                    float* l_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m_out || !l_out) return STARKV_EINVAL;
+  return starkv::decode_impl(args, workspace, workspace_bytes, (cudaStream_t)stream, true, cp_rank, cp_world, m_out,
+                             l_out);
 }
 
 int starkv_fold_q(const void* query, const int64_t q_stride[3], int32_t q_dtype, const void* k_up,

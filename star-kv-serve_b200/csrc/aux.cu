@@ -173,8 +173,12 @@ __global__ void __launch_bounds__(128) lift_kernel(const LiftParams p) {
   __shared__ __align__(16) __nv_bfloat16 vt[kLiftVT][kLiftLd];       // [v][d]
   if (tid < kLiftBT) {
     const int b = b0 + tid;
-    const float l = b < p.n ? p.l_seq[(int64_t)b * p.num_heads + h] : 0.f;
-    inv_l[tid] = l > 0.f ? 1.f / l : 0.f;   // empty sequence -> 0, as the reference
+    if (p.l_seq) {
+      const float l = b < p.n ? p.l_seq[(int64_t)b * p.num_heads + h] : 0.f;
+      inv_l[tid] = l > 0.f ? 1.f / l : 0.f;   // empty sequence -> 0, as the reference
+    } else {
+      inv_l[tid] = 1.f;                        // partial (context-parallel) output: unnormalised
+    }
   }
   // per-thread share of one staged step: 8 x float4 of pv, 16 bf16 of v_up
   float4 rp[8];

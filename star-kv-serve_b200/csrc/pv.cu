@@ -103,13 +103,13 @@ struct SubItem {
   int range, b, page0, npages;
 };
 
-__device__ __forceinline__ bool next_sub(int& u, int u_end, int total_pages, const int* pprefix, int n,
-                                         SubItem& si) {
+__device__ __forceinline__ bool next_sub(int& u, int u_end, int total_pages, const int* pprefix, const int* pbeg,
+                                         int n, SubItem& si) {
   if (u >= u_end) return false;
   si.range = u / total_pages;
   const int pi = u % total_pages;
   si.b = find_le(pprefix, n, pi);
-  si.page0 = pi - pprefix[si.b];
+  si.page0 = pi - pprefix[si.b] + pbeg[si.b];   // absolute page of the sequence
   const int seq_end = si.range * total_pages + pprefix[si.b + 1];
   const int e = min(u_end, seq_end);
   si.npages = e - u;
@@ -120,7 +120,7 @@ __device__ __forceinline__ bool next_sub(int& u, int u_end, int total_pages, con
 }  // namespace
 
 size_t pv_smem_bytes(bool quant, const PvParams& p) {
-  return (size_t)pv_layout(quant, p).total + (size_t)(p.n + 1) * 4;
+  return (size_t)pv_layout(quant, p).total + (size_t)(2 * p.n + 1) * 4;
 }
 
 template <bool QUANT>
@@ -130,7 +130,8 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const PvLayout LY = pv_layout(QUANT, p);
   PvCtl* ctl = reinterpret_cast<PvCtl*>(smem + LY.stages * LY.stage_bytes);
-  int* pprefix = reinterpret_cast<int*>(ctl + 1);   // [n+1] page prefix
+  int* pprefix = reinterpret_cast<int*>(ctl + 1);   // [n+1] page prefix over this rank's pages
+  int* pbeg = pprefix + p.n + 1;                     // [n] first page of this rank in each sequence
   volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = LY.stages;
@@ -140,7 +141,12 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     for (int b = 0; b < p.n; ++b) {
       pprefix[b] = acc;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
-      acc += (L + 15) >> 4;
+      // this rank's pages: those of its 256-token tiles [T r / w, T (r+1) / w)
+      const int T = (L + 255) >> 8;
+      const int s0 = (int)((int64_t)T * p.cp_rank / p.cp_world), s1 = (int)((int64_t)T * (p.cp_rank + 1) / p.cp_world);
+      const int pg0 = 16 * s0, pg1 = min(16 * s1, (L + 15) >> 4);
+      pbeg[b] = pg0;
+      acc += max(pg1 - pg0, 0);
     }
     pprefix[p.n] = acc;
     for (int s = 0; s < S; ++s) {
@@ -191,7 +197,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     int u = u_begin;
     SubItem si;
     bool stop = false;
-    while (!stop && next_sub(u, u_end, total_pages, pprefix, p.n, si)) {
+    while (!stop && next_sub(u, u_end, total_pages, pprefix, pbeg, p.n, si)) {
       const int mt0 = si.range * p.mt_per_range;
       const int mt1 = min(mt0 + p.mt_per_range, p.n_mtiles);
       const int pend = si.page0 + si.npages;
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
       uint32_t it = 0, acc_cnt = 0;
       int u = u_begin;
       SubItem si;
-      while (!*abort_flag && next_sub(u, u_end, total_pages, pprefix, p.n, si)) {
+      while (!*abort_flag && next_sub(u, u_end, total_pages, pprefix, pbeg, p.n, si)) {
         const int mt0 = si.range * p.mt_per_range;
         const int nmt = min(mt0 + p.mt_per_range, p.n_mtiles) - mt0;
         if (!mbar_wait(&ctl->accempty, (acc_cnt & 1) ^ 1, abort_flag, p.status)) break;
@@ -280,7 +286,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     int u = u_begin;
     SubItem si;
     bool ok = true;
-    while (ok && !*abort_flag && next_sub(u, u_end, total_pages, pprefix, p.n, si)) {
+    while (ok && !*abort_flag && next_sub(u, u_end, total_pages, pprefix, pbeg, p.n, si)) {
       const int b = si.b;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int mt0 = si.range * p.mt_per_range;

@@ -84,7 +84,7 @@ struct SharedCtl {
 
 // Shared memory carve-up (byte offsets from the 1024-aligned base).
 struct SmemLayout {
-  int cs, ab, codes, code_slot, sc, logits, red, tiles, prefix, ctl, total;
+  int cs, ab, codes, code_slot, sc, logits, red, tiles, prefix, sbeg, ctl, total;
 };
 
 __host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int k_width, int code_pitch,
@@ -101,7 +101,8 @@ __host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int 
   L.red = L.logits + H * (kTile + 1) * 4;
   L.tiles = (L.red + kEpiWarps * H * 4 + 15) & ~15;
   L.prefix = L.tiles + nc * (kChunk / 16) * 4;
-  L.ctl = (L.prefix + (n + 1) * 4 + 15) & ~15;
+  L.sbeg = L.prefix + (n + 1) * 4;
+  L.ctl = (L.sbeg + n * 4 + 15) & ~15;
   L.total = L.ctl + (int)sizeof(SharedCtl);
   return L;
 }
@@ -147,7 +148,8 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
   float* logits = reinterpret_cast<float*>(smem + SL.logits);    // [H][129]
   float* red_m = reinterpret_cast<float*>(smem + SL.red);        // [warps][H]
   int* tiles = reinterpret_cast<int*>(smem + SL.tiles);           // [NC * 8], -1 past NT
-  int* prefix = reinterpret_cast<int*>(smem + SL.prefix);         // [n+1]
+  int* prefix = reinterpret_cast<int*>(smem + SL.prefix);         // [n+1] item prefix over sequences
+  int* sbeg = reinterpret_cast<int*>(smem + SL.sbeg);             // [n] first 256-token tile of this rank
   SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem + SL.ctl);
   volatile int* abort_flag = &ctl->abort_flag;
 
@@ -162,7 +164,10 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     for (int b = 0; b < p.n; ++b) {
       prefix[b] = acc;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
-      acc += (L + kPairTokens - 1) / kPairTokens * p.group;
+      const int T = (L + kPairTokens - 1) / kPairTokens;     // 256-token tiles of the sequence
+      const int s0 = (int)((int64_t)T * p.cp_rank / p.cp_world), s1 = (int)((int64_t)T * (p.cp_rank + 1) / p.cp_world);
+      sbeg[b] = s0;
+      acc += (s1 - s0) * p.group;
     }
     prefix[p.n] = acc;
   }
@@ -230,7 +235,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     auto block_of = [&](int item) -> int {   // block id of page `lane` of an item (lanes 0-7)
       if (item >= total_items || lane >= 8) return 0;
       const int b = find_seq(prefix, p.n, item);
-      const int sup = (item - prefix[b]) / p.group;
+      const int sup = sbeg[b] + (item - prefix[b]) / p.group;
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int t = sup * kPairTokens + kTile * (int)rank + 16 * lane;
       if (t >= L) return 0;
@@ -258,7 +263,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         const int b = find_seq(prefix, p.n, item);
         const int rem = item - prefix[b];
         const int j = rem % p.group;
-        const int t0 = (rem / p.group) * kPairTokens + kTile * (int)rank;   // this CTA's first token
+        const int t0 = (sbeg[b] + rem / p.group) * kPairTokens + kTile * (int)rank;   // this CTA's first token
 #pragma unroll
         for (int pg = 0; pg < 8; ++pg) slot[pg] = (t0 + 16 * pg) % p.block_size;
         // rotary rows of this CTA's tokens: the pair MMA's A half
@@ -372,7 +377,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       const int b = find_seq(prefix, p.n, item);
       const int rem = item - prefix[b];
       const int j = rem % p.group;
-      const int tile = (rem / p.group) * 2 + (int)rank;   // this CTA's 128-token tile
+      const int tile = (sbeg[b] + rem / p.group) * 2 + (int)rank;   // this CTA's 128-token tile
       const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
       const int t0 = tile * kTile;
       if (QUANT && !mbar_wait(&ctl->sc_full, item_cnt & 1, abort_flag, p.status)) break;

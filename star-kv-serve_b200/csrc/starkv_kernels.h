@@ -42,6 +42,8 @@ struct ScoresParams {
   int code_pitch, tail_pitch;      // staged row pitch of a full / the last code window (bytes)
   int n_wins;                      // code windows per row
   int sc_pitch, sc_x0;             // 3.2-bit: staged scale window (pitch, 16-aligned byte start)
+  int cp_rank, cp_world;           // context split: this rank decodes its share of each sequence's
+                                   // 256-token tiles (rank r of w: tiles [T*r/w, T*(r+1)/w))
   __half* e16;
   float* m_tile;
   float* m_seq;
@@ -62,6 +64,7 @@ struct PvParams {
   int cache_dtype;
   // 3.2-bit V layout (paged_quant.QuantRow)
   int v_nout, v_nbo, v_bytes, vq_off, vs_off, vx0, v_boxes;
+  int cp_rank, cp_world;  // context split, as in ScoresParams (pages of the rank's 256-token tiles)
   int t_out;              // tiles over the outlier block (the rest cover inliers)
   const __half* e16;
   const float* m_tile;
@@ -76,7 +79,7 @@ struct PvParams {
 struct LiftParams {
   const float* pv;        // [n, H, pv_stride]
   int pv_stride;
-  const float* l_seq;
+  const float* l_seq;     // null: no normalisation (context-parallel partial output)
   const void* v_up; int64_t vu_s0, vu_s1, vu_s2; int v_up_dtype;   // [H, rv, Hd]
   void* out; int64_t o_s0, o_s1, o_s2; int out_dtype;              // [n, H, Hd]
   int n, num_heads, v_rank, head_dim;

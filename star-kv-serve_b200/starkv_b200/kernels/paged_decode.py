@@ -37,9 +37,15 @@ def paged_starkv_decode(
     *,
     out: torch.Tensor | None = None,
     ws: torch.Tensor | None = None,
-) -> torch.Tensor:
+    context: tuple[int, int] | None = None,
+):
     """Returns the attention output per query head, ``[n, H_q, head_dim]`` in
-    ``v_up_by_q.dtype`` (paged_decode.py:166)."""
+    ``v_up_by_q.dtype`` (paged_decode.py:166).
+
+    With ``context=(rank, world)`` the call decodes only this rank's share of every
+    sequence (context-parallel decode, starkv_b200.context_parallel) and returns
+    ``(out, m, l)``: ``out`` f32 ``[n, H, 128]`` unnormalised, ``m`` / ``l`` f32
+    ``[n, H]`` the rank's per-head logit max and softmax denominator."""
     n, num_heads, head_dim = query.shape
     num_kv_heads = k_ranks.numel()
     v_rank = v_up_by_q.shape[1]
@@ -47,10 +53,15 @@ def paged_starkv_decode(
     assert head_dim % 2 == 0 and num_heads % num_kv_heads == 0
     assert kv_cache.shape[-1] == k_width + v_rank, "cache width != K codes + V codes"
     assert cos_sin_cache.shape[-1] == head_dim and cos_sin_cache.shape[0] >= max_seq_len
+    if context is not None:
+        if out is None:
+            out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+        m_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+        l_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
     if out is None:
         out = torch.empty((n, num_heads, head_dim), dtype=v_up_by_q.dtype, device=query.device)
     if n == 0:
-        return out
+        return (out, m_out.fill_(float("-inf")), l_out.zero_()) if context is not None else out
     k_ranks = k_ranks if k_ranks.dtype == torch.int32 else k_ranks.to(torch.int32)
     k_head_offsets = k_head_offsets if k_head_offsets.dtype == torch.int32 else k_head_offsets.to(torch.int32)
     block_table = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
@@ -77,6 +88,12 @@ def paged_starkv_decode(
         _lib.i64s(cos_sin_cache.stride()), _lib.dtype_code(cos_sin_cache), cos_sin_cache.shape[0]
     a.scale = float(scale)
     a.out, a.out_stride, a.out_dtype = out.data_ptr(), _lib.i64s(out.stride()), _lib.dtype_code(out)
+    if context is not None:
+        rank, world = context
+        st = _lib.lib().starkv_paged_decode_bf16_partial(a, int(rank), int(world), m_out.data_ptr(), l_out.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), _lib.stream_ptr(query.device))
+        _lib.check(st, "paged_starkv_decode")
+        return out, m_out, l_out
     st = _lib.lib().starkv_paged_decode_bf16(a, ws.data_ptr(), ws.numel(), _lib.stream_ptr(query.device))
     _lib.check(st, "paged_starkv_decode")
     return out

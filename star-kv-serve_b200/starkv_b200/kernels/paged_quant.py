@@ -183,17 +183,28 @@ def paged_quant_decode(
     *,
     out: torch.Tensor | None = None,
     ws: torch.Tensor | None = None,
-) -> torch.Tensor:
-    """Returns the attention output per query head, ``[n, H, 128]`` in ``v_up_by_q.dtype``."""
+    context: tuple[int, int] | None = None,
+):
+    """Returns the attention output per query head, ``[n, H, 128]`` in ``v_up_by_q.dtype``.
+
+    With ``context=(rank, world)`` the call decodes only this rank's share of every
+    sequence (context-parallel decode, starkv_b200.context_parallel) and returns
+    ``(out, m, l)``: ``out`` f32 ``[n, H, 128]`` unnormalised, ``m`` / ``l`` f32
+    ``[n, H]`` the rank's per-head logit max and softmax denominator."""
     n, H, D = query.shape
     # the reference's own preconditions (paged_quant.py:374-376)
     assert D == HEAD_DIM and H == row.num_kv_heads, "4-bit decode: MHA, head_dim 128"
     assert kv_cache.dtype == torch.uint8 and kv_cache.shape[-1] == row.nbytes
     assert cos_sin_cache.shape[-1] == D and cos_sin_cache.shape[0] >= max_seq_len
+    if context is not None:
+        if out is None:
+            out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+        m_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+        l_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
     if out is None:
         out = torch.empty((n, H, D), dtype=v_up_by_q.dtype, device=query.device)
     if n == 0:
-        return out
+        return (out, m_out.fill_(float("-inf")), l_out.zero_()) if context is not None else out
     th, tn, tlast = k_tiles
     need = workspace.bytes_needed(n, H, H, row.k_width, row.v_rank, max_seq_len)
     if ws is None:
@@ -220,6 +231,12 @@ def paged_quant_decode(
     a.v_nout, a.v_nbo, a.v_bytes = row.v_nout, row.v_nbo, row.v_bytes
     a.head_of_lane = head_of_lane.data_ptr()
     a.tile_head, a.tile_nout, a.tile_last = th.data_ptr(), tn.data_ptr(), tlast.data_ptr()
+    if context is not None:
+        rank, world = context
+        st = _lib.lib().starkv_paged_decode_q32_partial(a, int(rank), int(world), m_out.data_ptr(), l_out.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), _lib.stream_ptr(query.device))
+        _lib.check(st, "paged_quant_decode")
+        return out, m_out, l_out
     st = _lib.lib().starkv_paged_decode_q32(a, ws.data_ptr(), ws.numel(), _lib.stream_ptr(query.device))
     _lib.check(st, "paged_quant_decode")
     return out

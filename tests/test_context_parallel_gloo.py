@@ -1,0 +1,102 @@
+"""Context-parallel decode, host side, on two gloo ranks (CPU): each rank takes its
+contiguous share of every sequence's 256-token tiles (the split the CUDA path
+uses), computes the partial (unnormalised lifted output, per-head max, softmax
+denominator) of the reference decode math over those tokens, and
+starkv_b200.context_parallel.combine over the process group must give the
+unsharded decode of the oracle. Sequence lengths include ones with fewer tiles
+than ranks (a rank with no token)."""
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+WORLD = 2
+LENS = [700, 31, 513, 256]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(seed=9, H=4):
+    import starkv_oracle as O
+    rng = np.random.default_rng(seed)
+    ranks = [16, 32, 48, 16]
+    _, offsets, W = O.k_layout(ranks)
+    rv, Lmax = 64, max(LENS)
+    seqs = []
+    for L in LENS:
+        k = rng.standard_normal((L, W))
+        for r, o in zip(ranks, offsets):
+            k[:, o + r:o + (-(-r // 16) * 16)] = 0.0
+        seqs.append((rng.standard_normal((H, 128)), k, rng.standard_normal((L, rv))))
+    k_up = rng.standard_normal((W, 128)) / 6
+    v_up = rng.standard_normal((H, rv, 128)) / 8
+    return ranks, offsets, seqs, k_up, v_up, O.rope_cos_sin(Lmax), 128 ** -0.5
+
+
+def _partial(q, k_rows, v_rows, k_up, ranks, offsets, v_up, cs, scale, t0, t1):
+    """Unnormalised lifted output, max and denominator over tokens [t0, t1)."""
+    H = q.shape[0]
+    out, m, l = np.zeros((H, 128)), np.full(H, -np.inf), np.zeros(H)
+    if t1 <= t0:
+        return out, m, l
+    cos, sin = cs[t0:t1, :64], cs[t0:t1, 64:]
+    for h in range(H):
+        o, r = offsets[h], ranks[h]
+        k = k_rows[t0:t1, o:o + r] @ k_up[o:o + r]
+        kr = np.concatenate([k[:, :64] * cos - k[:, 64:] * sin, k[:, 64:] * cos + k[:, :64] * sin], 1)
+        lg = kr @ q[h] * scale
+        m[h] = lg.max()
+        p = np.exp(lg - m[h])
+        l[h] = p.sum()
+        out[h] = (p @ v_rows[t0:t1]) @ v_up[h]
+    return out, m, l
+
+
+def _rank_main(rank, port, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60))
+    try:
+        import starkv_oracle as O
+        from starkv_b200.context_parallel import combine
+        ranks, offsets, seqs, k_up, v_up, cs, scale = _inputs()
+        outs, ms, ls = [], [], []
+        for (q, k, v), L in zip(seqs, LENS):
+            T = -(-L // 256)
+            s0, s1 = T * rank // WORLD, T * (rank + 1) // WORLD
+            o, m, l = _partial(q, k, v, k_up, ranks, offsets, v_up, cs, scale, 256 * s0, min(256 * s1, L))
+            outs.append(o); ms.append(m); ls.append(l)
+        got = combine(torch.tensor(np.stack(outs)), torch.tensor(np.stack(ms)), torch.tensor(np.stack(ls)),
+                      dtype=torch.float64).numpy()
+        if rank == 0:
+            ref = np.stack([O.attend_one(q, k, v, k_up, ranks, offsets, 1, v_up, cs, scale) for q, k, v in seqs])
+            result["err"] = float(np.abs(got - ref).max())
+            result["scale"] = float(np.abs(ref).max())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_context_split_matches_unsplit_decode():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_rank_main, args=(r, port, result)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=180)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert result["scale"] > 0
+        assert result["err"] <= 1e-10 * max(1.0, result["scale"]), result["err"]
