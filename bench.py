@@ -156,7 +156,8 @@ def run_step_fns(layer, device, cp=None):
     slots = (layer.block_table[torch.arange(n, device=device), pos // 16].long() * 16 + pos % 16)
     H = layer.num_heads
     ws = workspace.reserve(device, n, H, len(layer.ranks), layer.k_width, layer.v_rank, layer.max_seq_len)
-    out = torch.empty(n, H, 128, dtype=torch.float32 if cp else torch.bfloat16, device=device)
+    out = torch.empty(n, H, 128, dtype=torch.bfloat16, device=device)
+    part = torch.empty(n * H * 130, dtype=torch.float32, device=device) if cp else None
     # context split: the new token of every sequence lies in the last rank's share
     writes = cp is None or cp[0] == cp[1] - 1
     if cp is not None:
@@ -174,14 +175,14 @@ def run_step_fns(layer, device, cp=None):
                            layer.k_nouts)
             r = pq.paged_quant_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.row, layer.k_up,
                                       layer.head_of_lane, layer.k_tiles, layer.v_up_by_q, layer.cos_sin_cache,
-                                      layer.scale, out=out, ws=ws, context=cp)
+                                      layer.scale, out=out, ws=ws, context=cp, partial=part)
         else:
             if writes:
                 write_kv_bf16(kn, vn, layer.kv_cache, slots)
             r = paged_starkv_decode(q, layer.kv_cache, bt, sl, layer.max_seq_len, layer.k_up, layer.k_ranks,
                                     layer.k_head_offsets, layer.k_width, layer.v_up_by_q, layer.cos_sin_cache,
-                                    layer.scale, out=out, ws=ws, context=cp)
-        return combine(*r) if cp is not None else r
+                                    layer.scale, out=out, ws=ws, context=cp, partial=part)
+        return combine(*r, result=out) if cp is not None else r
     return step, (k_new, v_new)
 
 

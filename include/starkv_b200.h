@@ -150,6 +150,17 @@ STARKV_API int starkv_paged_decode_q32_partial(const StarKVDecodeArgs* args, int
                                                void* stream);
 
 /*
+ * Combine of context-parallel partials (no counterpart in the reference):
+ * parts holds `world` packed partials one after the other, each
+ *   out f32 [n, H, 128] | m f32 [n, H] | l f32 [n, H]   (n*H*130 floats)
+ * as written by the *_partial calls into one buffer (starkv_b200.context_parallel
+ * gathers them from the ranks). Writes the combined [n, H, 128] output (strides in
+ * elements, bf16 / f16 / f32): sum_r exp(m_r - M) out_r / sum_r exp(m_r - M) l_r.
+ */
+STARKV_API int starkv_cp_combine(const float* parts, int32_t world, int32_t n, int32_t num_heads, void* out,
+                                 const int64_t out_stride[3], int32_t out_dtype, void* stream);
+
+/*
  * paged_quant.py:241-255 (fold_q): q [n, H, 128] (RoPE applied), k_up [W, 128],
  * head_of_lane [W] -> ab [n, W, 128] f16 (contiguous), the logit scale folded in:
  *   A[r,i] = (q_i U[r,i] + q_{i+64} U[r,i+64]) * scale

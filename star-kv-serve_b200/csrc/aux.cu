@@ -428,3 +428,45 @@ extern "C" int starkv_cache_write_bf16(const StarKVCacheWriteArgs* a, void* stre
   cache_write_kernel<<<a->n, 256, 0, (cudaStream_t)stream>>>(*a);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
+
+// ---------------------------------------------------------------------------
+// context-parallel combine: parts = world packed partials, each
+//   [n, H, 128] out_r | [n, H] m_r | [n, H] l_r   (f32, rank-major)
+// out[b, h, :] = sum_r exp(m_r - M) out_r / sum_r exp(m_r - M) l_r, M = max_r m_r
+// (0 when no rank holds a token of the sequence, as the reference's empty case)
+// ---------------------------------------------------------------------------
+namespace starkv {
+
+__global__ void __launch_bounds__(128) cp_combine_kernel(const float* __restrict__ parts, int world, int n, int H,
+                                                         void* out, int64_t o0, int64_t o1, int64_t o2, int out_dtype) {
+  const int bh = blockIdx.x;                 // (b, h)
+  const int d = threadIdx.x;                 // 0..127
+  const int64_t nh = (int64_t)n * H;
+  const int64_t part = nh * 130;
+  float M = -INFINITY;
+  for (int r = 0; r < world; ++r) M = fmaxf(M, parts[r * part + nh * 128 + bh]);
+  float num = 0.f, den = 0.f;
+  if (M > -INFINITY) {
+    for (int r = 0; r < world; ++r) {
+      const float* pr = parts + r * part;
+      const float s = __expf(pr[nh * 128 + bh] - M);
+      num += s * pr[(int64_t)bh * 128 + d];
+      den += s * pr[nh * 129 + bh];
+    }
+  }
+  const int b = bh / H, h = bh - b * H;
+  store_elem(out, (int64_t)b * o0 + (int64_t)h * o1 + (int64_t)d * o2, out_dtype, den > 0.f ? num / den : 0.f);
+}
+
+}  // namespace starkv
+
+extern "C" int starkv_cp_combine(const float* parts, int32_t world, int32_t n, int32_t num_heads, void* out,
+                                 const int64_t out_stride[3], int32_t out_dtype, void* stream) {
+  using namespace starkv;
+  if (!parts || !out || !out_stride || world < 1 || n < 0 || num_heads <= 0) return STARKV_EINVAL;
+  if (out_dtype != STARKV_BF16 && out_dtype != STARKV_F16 && out_dtype != STARKV_F32) return STARKV_EDTYPE;
+  if (n == 0) return STARKV_OK;
+  cp_combine_kernel<<<n * num_heads, 128, 0, (cudaStream_t)stream>>>(parts, world, n, num_heads, out, out_stride[0],
+                                                                     out_stride[1], out_stride[2], out_dtype);
+  return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
+}

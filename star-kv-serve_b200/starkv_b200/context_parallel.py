@@ -8,38 +8,79 @@ combined exactly:
 
 (out_r is the rank's unnormalised, already lifted output, m_r / l_r its per-head
 logit max and softmax denominator). Every rank reads 1/world of the K and V codes,
-including the V latent that head sharding has to replicate. The exchange is one
-MAX all-reduce of [n, H] and one SUM all-reduce of [n, H, 129] f32 (about 1 MB for
-64 sequences x 32 heads).
+including the V latent that head sharding has to replicate.
+
+A rank's partial lives in one packed f32 buffer ``[out n*H*128 | m n*H | l n*H]``;
+the exchange is a single NCCL all-gather of those buffers (about 1 MB each for 64
+sequences x 32 heads) and the combination one native kernel
+(``starkv_cp_combine``).
 """
 from __future__ import annotations
 
 import torch
 
+from . import _lib
 
-def _normalise(buf: torch.Tensor, dtype) -> torch.Tensor:
-    num, den = buf[..., :-1], buf[..., -1:]
-    return torch.where(den > 0, num / den.clamp_min(torch.finfo(torch.float32).tiny), torch.zeros_like(num)).to(dtype)
+_PACK = 130   # floats per (sequence, head): 128 output values, max, denominator
 
 
-def combine(out: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=None, dtype=torch.bfloat16) -> torch.Tensor:
-    """All ranks of `group` call this with their partial (out, m, l); every rank gets
-    the combined [n, H, 128] output in `dtype`."""
+def partial_views(n: int, H: int, device, buf: torch.Tensor | None = None):
+    """(out [n, H, 128], m [n, H], l [n, H]) views of one packed f32 buffer."""
+    size = n * H * _PACK
+    if buf is None:
+        buf = torch.empty(size, dtype=torch.float32, device=device)
+    assert buf.dtype == torch.float32 and buf.is_contiguous() and buf.numel() >= size
+    nh = n * H
+    return (buf[:nh * 128].view(n, H, 128), buf[nh * 128:nh * 129].view(n, H), buf[nh * 129:nh * 130].view(n, H))
+
+
+def _packed(out: torch.Tensor, m: torch.Tensor, l: torch.Tensor) -> torch.Tensor:
+    n, H = m.shape
+    nh = n * H
+    if (out.is_contiguous() and m.is_contiguous() and l.is_contiguous()
+            and m.data_ptr() == out.data_ptr() + 4 * nh * 128 and l.data_ptr() == m.data_ptr() + 4 * nh):
+        return torch.as_strided(out, (nh * _PACK,), (1,))
+    return torch.cat([out.reshape(-1), m.reshape(-1), l.reshape(-1)])
+
+
+def _combine_parts(parts: torch.Tensor, world: int, n: int, H: int, dtype, result=None) -> torch.Tensor:
+    if result is None:
+        result = torch.empty((n, H, 128), dtype=dtype, device=parts.device)
+    st = _lib.lib().starkv_cp_combine(parts.data_ptr(), world, n, H, result.data_ptr(), _lib.i64s(result.stride()),
+                                      _lib.dtype_code(result), _lib.stream_ptr(parts.device))
+    _lib.check(st, "cp_combine")
+    return result
+
+
+_gather_bufs: dict = {}
+
+
+def gather_partials(out: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=None) -> torch.Tensor:
+    """All ranks of `group`: one all-gather of the packed partials; returns the
+    rank-major buffer [world * n*H*130] (reused between calls of the same size)."""
     import torch.distributed as dist
-    M = m.clone()
-    dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)
-    s = torch.exp(m - M)                                   # 0 where this rank has no token
-    buf = torch.cat([out * s.unsqueeze(-1), (l * s).unsqueeze(-1)], -1)
-    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
-    return _normalise(buf, dtype)
+    world = dist.get_world_size(group)
+    local = _packed(out, m, l)
+    key = (local.device, local.dtype, world, local.numel())
+    gathered = _gather_bufs.get(key)
+    if gathered is None:
+        gathered = _gather_bufs[key] = torch.empty(world * local.numel(), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(gathered, local, group=group)
+    return gathered
+
+
+def combine(out: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=None, dtype=torch.bfloat16,
+            result: torch.Tensor | None = None) -> torch.Tensor:
+    """All ranks of `group` call this with their partial (out, m, l) on the GPU;
+    every rank gets the combined [n, H, 128] output in `dtype`."""
+    import torch.distributed as dist
+    n, H = m.shape
+    gathered = gather_partials(out, m, l, group)
+    return _combine_parts(gathered, dist.get_world_size(group), n, H, dtype, result)
 
 
 def combine_local(parts: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]], dtype=torch.bfloat16) -> torch.Tensor:
     """The same combination for partial results held by one process (tests, one GPU)."""
-    M = torch.stack([m for _, m, _ in parts]).amax(0)
-    buf = None
-    for out, m, l in parts:
-        s = torch.exp(m - M)
-        t = torch.cat([out * s.unsqueeze(-1), (l * s).unsqueeze(-1)], -1)
-        buf = t if buf is None else buf + t
-    return _normalise(buf, dtype)
+    n, H = parts[0][1].shape
+    stacked = torch.cat([_packed(*p) for p in parts])
+    return _combine_parts(stacked, len(parts), n, H, dtype)

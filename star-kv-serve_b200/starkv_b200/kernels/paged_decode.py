@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import _lib, workspace
+from .. import _lib, context_parallel, workspace
 
 # Kept for call-site compatibility with the reference (paged_decode.py:22-28);
 # the tile shapes of this implementation are fixed inside the library.
@@ -38,6 +38,7 @@ def paged_starkv_decode(
     out: torch.Tensor | None = None,
     ws: torch.Tensor | None = None,
     context: tuple[int, int] | None = None,
+    partial: torch.Tensor | None = None,
 ):
     """Returns the attention output per query head, ``[n, H_q, head_dim]`` in
     ``v_up_by_q.dtype`` (paged_decode.py:166).
@@ -45,7 +46,9 @@ def paged_starkv_decode(
     With ``context=(rank, world)`` the call decodes only this rank's share of every
     sequence (context-parallel decode, starkv_b200.context_parallel) and returns
     ``(out, m, l)``: ``out`` f32 ``[n, H, 128]`` unnormalised, ``m`` / ``l`` f32
-    ``[n, H]`` the rank's per-head logit max and softmax denominator."""
+    ``[n, H]`` the rank's per-head logit max and softmax denominator.
+    The three are views of one packed f32 buffer (``partial``, allocated when not
+    given; see ``context_parallel.partial_views``)."""
     n, num_heads, head_dim = query.shape
     num_kv_heads = k_ranks.numel()
     v_rank = v_up_by_q.shape[1]
@@ -54,10 +57,7 @@ def paged_starkv_decode(
     assert kv_cache.shape[-1] == k_width + v_rank, "cache width != K codes + V codes"
     assert cos_sin_cache.shape[-1] == head_dim and cos_sin_cache.shape[0] >= max_seq_len
     if context is not None:
-        if out is None:
-            out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
-        m_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
-        l_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+        out, m_out, l_out = context_parallel.partial_views(query.shape[0], query.shape[1], query.device, partial)
     if out is None:
         out = torch.empty((n, num_heads, head_dim), dtype=v_up_by_q.dtype, device=query.device)
     if n == 0:

@@ -24,7 +24,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .. import _lib, workspace
+from .. import _lib, context_parallel, workspace
 
 OUTLIER_RATIO = 0.2
 HADAMARD_SEED = 1234
@@ -184,23 +184,23 @@ def paged_quant_decode(
     out: torch.Tensor | None = None,
     ws: torch.Tensor | None = None,
     context: tuple[int, int] | None = None,
+    partial: torch.Tensor | None = None,
 ):
     """Returns the attention output per query head, ``[n, H, 128]`` in ``v_up_by_q.dtype``.
 
     With ``context=(rank, world)`` the call decodes only this rank's share of every
     sequence (context-parallel decode, starkv_b200.context_parallel) and returns
     ``(out, m, l)``: ``out`` f32 ``[n, H, 128]`` unnormalised, ``m`` / ``l`` f32
-    ``[n, H]`` the rank's per-head logit max and softmax denominator."""
+    ``[n, H]`` the rank's per-head logit max and softmax denominator.
+    The three are views of one packed f32 buffer (``partial``, allocated when not
+    given; see ``context_parallel.partial_views``)."""
     n, H, D = query.shape
     # the reference's own preconditions (paged_quant.py:374-376)
     assert D == HEAD_DIM and H == row.num_kv_heads, "4-bit decode: MHA, head_dim 128"
     assert kv_cache.dtype == torch.uint8 and kv_cache.shape[-1] == row.nbytes
     assert cos_sin_cache.shape[-1] == D and cos_sin_cache.shape[0] >= max_seq_len
     if context is not None:
-        if out is None:
-            out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
-        m_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
-        l_out = torch.empty(query.shape[:2], dtype=torch.float32, device=query.device)
+        out, m_out, l_out = context_parallel.partial_views(query.shape[0], query.shape[1], query.device, partial)
     if out is None:
         out = torch.empty((n, H, D), dtype=v_up_by_q.dtype, device=query.device)
     if n == 0:

@@ -1,9 +1,11 @@
 """Context-parallel decode, host side, on two gloo ranks (CPU): each rank takes its
 contiguous share of every sequence's 256-token tiles (the split the CUDA path
-uses), computes the partial (unnormalised lifted output, per-head max, softmax
-denominator) of the reference decode math over those tokens, and
-starkv_b200.context_parallel.combine over the process group must give the
-unsharded decode of the oracle. Sequence lengths include ones with fewer tiles
+uses) and computes the partial (unnormalised lifted output, per-head max, softmax
+denominator) of the reference decode math over those tokens. The partials are
+exchanged with starkv_b200.context_parallel.gather_partials (one all-gather of
+packed [out | m | l] buffers), and the combination the native combine kernel
+applies (tested on the GPU), done here on the gathered data, must give the
+unsplit decode of the oracle. Sequence lengths include ones with fewer tiles
 than ranks (a rank with no token)."""
 import os
 import socket
@@ -66,7 +68,7 @@ def _rank_main(rank, port, result):
     dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60))
     try:
         import starkv_oracle as O
-        from starkv_b200.context_parallel import combine
+        from starkv_b200.context_parallel import gather_partials
         ranks, offsets, seqs, k_up, v_up, cs, scale = _inputs()
         outs, ms, ls = [], [], []
         for (q, k, v), L in zip(seqs, LENS):
@@ -74,9 +76,18 @@ def _rank_main(rank, port, result):
             s0, s1 = T * rank // WORLD, T * (rank + 1) // WORLD
             o, m, l = _partial(q, k, v, k_up, ranks, offsets, v_up, cs, scale, 256 * s0, min(256 * s1, L))
             outs.append(o); ms.append(m); ls.append(l)
-        got = combine(torch.tensor(np.stack(outs)), torch.tensor(np.stack(ms)), torch.tensor(np.stack(ls)),
-                      dtype=torch.float64).numpy()
+        parts = gather_partials(torch.tensor(np.stack(outs)), torch.tensor(np.stack(ms)),
+                                torch.tensor(np.stack(ls))).numpy()
         if rank == 0:
+            # the combination starkv_cp_combine applies, on the gathered rank-major packed buffer
+            n, H = len(LENS), ms[0].shape[0]
+            P = parts.reshape(WORLD, -1)
+            o = P[:, :n * H * 128].reshape(WORLD, n, H, 128)
+            m = P[:, n * H * 128:n * H * 129].reshape(WORLD, n, H)
+            l = P[:, n * H * 129:].reshape(WORLD, n, H)
+            M = m.max(0)
+            s = np.exp(m - M)
+            got = (s[..., None] * o).sum(0) / (s * l).sum(0)[..., None]
             ref = np.stack([O.attend_one(q, k, v, k_up, ranks, offsets, 1, v_up, cs, scale) for q, k, v in seqs])
             result["err"] = float(np.abs(got - ref).max())
             result["scale"] = float(np.abs(ref).max())
