@@ -16,6 +16,26 @@ namespace starkv {
 
 constexpr int kFoldLanes = 16;   // K lanes per 128-thread block (8 threads x 8 values each)
 
+// 8 consecutive elements (stride `st`) as floats: one or two 16-byte loads when the
+// run is contiguous and aligned, scalar loads otherwise.
+template <class T>
+__device__ __forceinline__ void load8(const T* p, int64_t st, float (&v)[8]) {
+  if (st == 1 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    if constexpr (sizeof(T) == 2) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = to_f32(e[k]);
+    } else {
+      const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = to_f32(p[(int64_t)k * st]);
+  }
+}
+
 template <class TQ, class TU>
 __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fold_blocks, int n_cs_blocks) {
   const int bid = blockIdx.x;
@@ -61,19 +81,14 @@ __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fol
       const int hq = head * p.group + j;
       const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)hq * p.q_s1;
       const TU* up = reinterpret_cast<const TU*>(p.k_up) + (int64_t)r * p.ku_s0;
-      TQ q0[8], q1[8];
-      TU u0[8], u1[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {   // all loads first, so they are in flight together
-        const int i = i0 + k;
-        q0[k] = qp[(int64_t)i * p.q_s2];
-        q1[k] = qp[(int64_t)(i + 64) * p.q_s2];
-        u0[k] = up[(int64_t)i * p.ku_s1];
-        u1[k] = up[(int64_t)(i + 64) * p.ku_s1];
-      }
+      float q0[8], q1[8], u0[8], u1[8];
+      load8(qp + (int64_t)i0 * p.q_s2, p.q_s2, q0);
+      load8(qp + (int64_t)(i0 + 64) * p.q_s2, p.q_s2, q1);
+      load8(up + (int64_t)i0 * p.ku_s1, p.ku_s1, u0);
+      load8(up + (int64_t)(i0 + 64) * p.ku_s1, p.ku_s1, u1);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float a0 = to_f32(q0[k]), a1 = to_f32(q1[k]), w0 = to_f32(u0[k]), w1 = to_f32(u1[k]);
+        const float a0 = q0[k], a1 = q1[k], w0 = u0[k], w1 = u1[k];
         av[k] = __float2half_rn((a0 * w0 + a1 * w1) * p.scale);
         bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
       }
@@ -95,15 +110,25 @@ __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fol
   }
   if (bid < n_fold_blocks + n_cs_blocks) {
     // rotary table rows -> f16 (zero past the table / max_seq_len), written as the
-    // 128-byte-swizzled K-major tiles the score MMA reads as its A operand
+    // 128-byte-swizzled K-major tiles the score MMA reads as its A operand; thread =
+    // one 16-byte unit (8 columns) of a row
     const int64_t e = (int64_t)(bid - n_fold_blocks) * 128 + threadIdx.x;
-    const int64_t row = e >> 7;
-    const int col = (int)(e & 127);
+    const int64_t row = e >> 4;
+    const int u = (int)(e & 15), col0 = u * 8;
     if (row >= p.l_pad) return;
-    float v = 0.f;
-    if (row < p.cs_rows && row < p.max_seq_len) v = load_elem(p.cs, row * p.cs_s0 + col * p.cs_s1, p.cs_dtype);
-    const int t = (int)(row & 127), kh = col >> 6, unit = ((col & 63) >> 3) ^ (t & 7);
-    p.cs16[((row >> 7) << 14) + kh * 8192 + t * 64 + unit * 8 + (col & 7)] = __float2half_rn(v);
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (row < p.cs_rows && row < p.max_seq_len) {
+      with_float_type(p.cs_dtype, [&](auto tc) {
+        using TC = decltype(tc);
+        load8(reinterpret_cast<const TC*>(p.cs) + row * p.cs_s0 + (int64_t)col0 * p.cs_s1, p.cs_s1, v);
+      });
+    }
+    __align__(16) __half hv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) hv[k] = __float2half_rn(v[k]);
+    const int t = (int)(row & 127), kh = u >> 3, unit = (u & 7) ^ (t & 7);
+    *reinterpret_cast<uint4*>(p.cs16 + ((row >> 7) << 14) + kh * 8192 + t * 64 + unit * 8) =
+        *reinterpret_cast<const uint4*>(hv);
     return;
   }
   // init: sequence max = -inf, pv = 0
@@ -123,7 +148,7 @@ int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream) {
   (void)quant;
   const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
   const int n_fold = p.n * p.group * lanes_per_seq;
-  const int n_cs = (int)(((int64_t)p.l_pad * 128 + 127) / 128);
+  const int n_cs = (int)(((int64_t)p.l_pad * 16 + 127) / 128);   // one thread per 16-byte unit
   const int n_init = 296;
   with_float_type(p.q_dtype, [&](auto tq) {
     with_float_type(p.k_up_dtype, [&](auto tu) {
@@ -161,23 +186,31 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+constexpr int kLiftGroups = 4;   // warp groups splitting the V channels of a block
+constexpr int kLiftPvtFloats = kLiftBT * (kLiftVT + 4);
+constexpr int kLiftGroupBytes = kLiftPvtFloats * 4 + kLiftVT * kLiftLd * 2;
+constexpr int kLiftSmem = kLiftGroups * kLiftGroupBytes + kLiftBT * 4;
+
 template <class TV>
-__global__ void __launch_bounds__(128) lift_kernel(const LiftParams p) {
+__global__ void __launch_bounds__(128 * kLiftGroups) lift_kernel(const LiftParams p) {
   const int h = blockIdx.x;
   const int d0 = blockIdx.y * 32;
   const int b0 = blockIdx.z * kLiftBT;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = threadIdx.x >> 7;             // this group's V steps: grp, grp + 4, ...
+  const int tid = threadIdx.x & 127, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  __shared__ float inv_l[kLiftBT];
-  __shared__ __align__(16) float pvt[kLiftBT][kLiftVT + 4];          // [b][v], padded rows
-  __shared__ __align__(16) __nv_bfloat16 vt[kLiftVT][kLiftLd];       // [v][d]
-  if (tid < kLiftBT) {
-    const int b = b0 + tid;
+  extern __shared__ __align__(16) uint8_t lift_smem[];
+  float (*pvt)[kLiftVT + 4] = reinterpret_cast<float (*)[kLiftVT + 4]>(lift_smem + grp * kLiftGroupBytes);   // [b][v]
+  __nv_bfloat16 (*vt)[kLiftLd] =
+      reinterpret_cast<__nv_bfloat16 (*)[kLiftLd]>(lift_smem + grp * kLiftGroupBytes + kLiftPvtFloats * 4);  // [v][d]
+  float* inv_l = reinterpret_cast<float*>(lift_smem + kLiftGroups * kLiftGroupBytes);
+  if (threadIdx.x < kLiftBT) {
+    const int b = b0 + threadIdx.x;
     if (p.l_seq) {
       const float l = b < p.n ? p.l_seq[(int64_t)b * p.num_heads + h] : 0.f;
-      inv_l[tid] = l > 0.f ? 1.f / l : 0.f;   // empty sequence -> 0, as the reference
+      inv_l[threadIdx.x] = l > 0.f ? 1.f / l : 0.f;   // empty sequence -> 0, as the reference
     } else {
-      inv_l[tid] = 1.f;                        // partial (context-parallel) output: unnormalised
+      inv_l[threadIdx.x] = 1.f;                        // partial (context-parallel) output: unnormalised
     }
   }
   // per-thread share of one staged step: 8 x float4 of pv, 16 bf16 of v_up
@@ -218,17 +251,21 @@ __global__ void __launch_bounds__(128) lift_kernel(const LiftParams p) {
       vt[vv][dd] = __float2bfloat16_rn(in ? to_f32(rv[i]) : 0.f);
     }
   };
+  // named barrier per group (ids 1..4; 128 threads each)
+  auto group_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(grp + 1) : "memory"); };
   const int rA = 16 * warp + g, rB = rA + 8;   // rows within the block's 64 sequences
   float acc[4][4] = {};
-  fetch(0);
+  const int vstride = kLiftVT * kLiftGroups;
+  const int vfirst = kLiftVT * grp;
+  if (vfirst < p.v_rank) fetch(vfirst);
   __syncthreads();   // inv_l ready
   const float sA = inv_l[rA], sB = inv_l[rB];
-  for (int v0 = 0; v0 < p.v_rank; v0 += kLiftVT) {
-    __syncthreads();
+  for (int v0 = vfirst; v0 < p.v_rank; v0 += vstride) {
+    group_sync();
     vbase = vnext;
     stash();
-    __syncthreads();
-    if (v0 + kLiftVT < p.v_rank) fetch(v0 + kLiftVT);   // next step's loads overlap this step's MMAs
+    group_sync();
+    if (v0 + vstride < p.v_rank) fetch(v0 + vstride);   // next step's loads overlap this step's MMAs
 #pragma unroll
     for (int ks = 0; ks < kLiftVT / 16; ++ks) {
       const int c0 = ks * 16 + 2 * t, c1 = c0 + 8;
@@ -240,11 +277,11 @@ __global__ void __launch_bounds__(128) lift_kernel(const LiftParams p) {
                           xa1.x * sA, xa1.y * sA, xb1.x * sB, xb1.y * sB};
       uint32_t hi[4], lo[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float e0 = x[2 * j], e1 = x[2 * j + 1];
+      for (int jj = 0; jj < 4; ++jj) {
+        const float e0 = x[2 * jj], e1 = x[2 * jj + 1];
         const float h0 = __bfloat162float(__float2bfloat16_rn(e0)), h1 = __bfloat162float(__float2bfloat16_rn(e1));
-        hi[j] = pack_bf16x2(h0, h1);
-        lo[j] = pack_bf16x2(e0 - h0, e1 - h1);
+        hi[jj] = pack_bf16x2(h0, h1);
+        lo[jj] = pack_bf16x2(e0 - h0, e1 - h1);
       }
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
@@ -259,23 +296,49 @@ __global__ void __launch_bounds__(128) lift_kernel(const LiftParams p) {
       }
     }
   }
+  // reduce the groups' partial sums through shared memory (reusing the staging area)
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(lift_smem);   // [group - 1][16][128]
+  if (grp > 0) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) red[((grp - 1) * 16 + nt * 4 + k) * 128 + tid] = acc[nt][k];
+  }
+  __syncthreads();
+  if (grp > 0) return;
+#pragma unroll
+  for (int gg = 0; gg < kLiftGroups - 1; ++gg)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[nt][k] += red[(gg * 16 + nt * 4 + k) * 128 + tid];
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
     const int d = d0 + nt * 8 + 2 * t;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int b = b0 + (j ? rB : rA);
+    for (int jj = 0; jj < 2; ++jj) {
+      const int b = b0 + (jj ? rB : rA);
       if (b >= p.n) continue;
       const int64_t o = (int64_t)b * p.o_s0 + (int64_t)h * p.o_s1;
-      if (d < p.head_dim) store_elem(p.out, o + (int64_t)d * p.o_s2, p.out_dtype, acc[nt][2 * j]);
-      if (d + 1 < p.head_dim) store_elem(p.out, o + (int64_t)(d + 1) * p.o_s2, p.out_dtype, acc[nt][2 * j + 1]);
+      if (d < p.head_dim) store_elem(p.out, o + (int64_t)d * p.o_s2, p.out_dtype, acc[nt][2 * jj]);
+      if (d + 1 < p.head_dim) store_elem(p.out, o + (int64_t)(d + 1) * p.o_s2, p.out_dtype, acc[nt][2 * jj + 1]);
     }
   }
 }
 
 int launch_lift(const LiftParams& p, cudaStream_t stream) {
   dim3 grid(p.num_heads, (p.head_dim + 31) / 32, (p.n + kLiftBT - 1) / kLiftBT);
-  with_float_type(p.v_up_dtype, [&](auto tv) { lift_kernel<decltype(tv)><<<grid, 128, 0, stream>>>(p); });
+  int st = STARKV_OK;
+  with_float_type(p.v_up_dtype, [&](auto tv) {
+    auto fn = lift_kernel<decltype(tv)>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLiftSmem) != cudaSuccess) {
+      st = STARKV_ECUDA;
+      return;
+    }
+    fn<<<grid, 128 * kLiftGroups, kLiftSmem, stream>>>(p);
+  });
+  if (st) return st;
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 
