@@ -10,9 +10,12 @@
 // channels, N = heads (rounded to 16), K = 16 tokens (one page) per instruction,
 // f32 accumulators in TMEM across the whole token range.
 //   bf16 codes: A = V^T straight from the TMA page tile (MN-major, 128 B swizzle).
-//   3.2-bit codes: worker warps dequantize nibbles to integer-valued f16 (n - 8,
-//   exact) into an MN-major A tile; the per-token scale folds into P (one P per
-//   outlier / inlier block, as paged_quant.py:320-346 does), so A stays exact.
+//   3.2-bit codes: worker warps turn each nibble n into the exact f16 n - 8 (even
+//   channels) or 16 (n - 8) (odd channels): one bit operation per channel pair
+//   makes 1024 + n or 1024 + 16 n, one f16 subtraction removes the bias exactly;
+//   the flush scales odd-channel rows by 1/16. The per-token scale folds into P
+//   (one P per outlier / inlier block, as paged_quant.py:320-346 does), so A
+//   stays exact.
 // P = e16 * exp(m_tile - m_seq) is built per page by the worker warps.
 //
 // Work split: the pages of all sequences are concatenated and cut into equal
@@ -294,13 +297,46 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
       const float* mtb = p.m_tile + (int64_t)b * p.num_heads * p.n_tiles;
       const float* msb = p.m_seq + (int64_t)b * p.num_heads;
       float lsum[4] = {0.f, 0.f, 0.f, 0.f};   // sum of P of this thread's (head, 4-token) tasks
-      // per-head tile max of the next page, loaded one page ahead (tile = 8 pages)
-      float mseq[4], mt_next[4];
+      // 3.2-bit dequant tasks of this thread (the same on every page): (M-tile, token,
+      // 16-byte window = 32 channels) -> the two aligned staged chunks it spans, the
+      // byte shift that cuts the window out of them, and its A-tile destination
+      constexpr int kMaxDq = 3;
+      int dq_src0[kMaxDq], dq_src1[kMaxDq], dq_dst[kMaxDq], dq_sh[kMaxDq];
+      int ndq = 0;
+      if (QUANT) {
+        const int nvq = p.v_boxes * 8 - 1;    // last staged 16-byte chunk index
+#pragma unroll
+        for (int i = 0; i < kMaxDq; ++i) {
+          const int task = wt + kWorkerThreads * i;
+          dq_src0[i] = dq_src1[i] = dq_dst[i] = dq_sh[i] = 0;
+          if (task >= nmt * 64) continue;
+          ndq = i + 1;
+          const int m = task >> 6, tt = task & 63;
+          const int k = tt & 15, j = tt >> 4;
+          const int gm = mt0 + m;
+          const bool outl = gm < p.t_out;
+          const int jt = outl ? gm : gm - p.t_out;
+          const int bb = (outl ? p.vq_off : p.vq_off + p.v_nbo) - p.vx0;   // block start in the staged row
+          const int win = bb + 64 * jt + 16 * j;
+          const int c0 = min(win >> 4, nvq), c1 = min((win >> 4) + 1, nvq);
+          dq_src0[i] = k * 128 + (c0 >> 3) * 2048 + (((c0 & 7) ^ (k & 7)) << 4);
+          dq_src1[i] = k * 128 + (c1 >> 3) * 2048 + (((c1 & 7) ^ (k & 7)) << 4);
+          dq_dst[i] = LY.v_bytes + m * 4096 + (k >> 3) * 2048 + (4 * j) * 128 + (k & 7) * 16;
+          dq_sh[i] = (bb & 15) * 8;   // bit offset of the window inside the 32 staged bytes
+        }
+      }
+      // P = e16 * exp(m_tile - m_seq): the factor of the current 128-token tile (8 pages),
+      // and the next tile's max loaded as soon as the current tile starts, so its
+      // latency is covered by 8 pages of work
+      int cur_tile = (si.page0 * 16) >> 7;
+      const int last_tile = ((si.page0 + si.npages - 1) * 16) >> 7;
+      float mseq[4], f_cur[4], mt_nt[4];
 #pragma unroll
       for (int tk = 0; tk < 4; ++tk) {
         const int h = min((wt + kWorkerThreads * tk) >> 2, p.num_heads - 1);
         mseq[tk] = msb[h];
-        mt_next[tk] = mtb[(int64_t)h * p.n_tiles + ((si.page0 * 16) >> 7)];
+        f_cur[tk] = __expf(mtb[(int64_t)h * p.n_tiles + cur_tile] - mseq[tk]);
+        mt_nt[tk] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
       }
       for (int pg = 0; pg < si.npages; ++pg, ++it) {
         const int s = it % S;
@@ -310,18 +346,24 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
         uint8_t* pb = st + LY.v_bytes + LY.a_bytes + LY.e_bytes;
         const uint8_t* es = st + LY.v_bytes + LY.a_bytes;   // e16 [heads][16 tokens]
         const int t0 = (si.page0 + pg) * 16;
-        const int next_tile = ((si.page0 + min(pg + 1, si.npages - 1)) * 16) >> 7;
+        if ((t0 >> 7) != cur_tile) {   // entering the next tile (uniform across the CTA)
+          cur_tile = t0 >> 7;
+#pragma unroll
+          for (int tk = 0; tk < 4; ++tk) {
+            const int h = min((wt + kWorkerThreads * tk) >> 2, p.num_heads - 1);
+            f_cur[tk] = __expf(mt_nt[tk] - mseq[tk]);
+            mt_nt[tk] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
+          }
+        }
         // P rows: thread -> (head, 4 consecutive tokens)
 #pragma unroll
         for (int tk = 0; tk < 4; ++tk) {
           const int task = wt + kWorkerThreads * tk;
           if (task >= p.nh * 4) break;
           const int h = task >> 2, kq = task & 3;
-          const float mt = mt_next[tk];
-          mt_next[tk] = mtb[(int64_t)min(h, p.num_heads - 1) * p.n_tiles + next_tile];
           float pv4[4] = {0.f, 0.f, 0.f, 0.f};
           if (h < p.num_heads) {
-            const float f = __expf(mt - mseq[tk]);
+            const float f = f_cur[tk];
             const uint2 raw = *reinterpret_cast<const uint2*>(es + h * 32 + 8 * kq);
             const __half2 e01 = *reinterpret_cast<const __half2*>(&raw.x);
             const __half2 e23 = *reinterpret_cast<const __half2*>(&raw.y);
@@ -343,7 +385,9 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
                 const uint16_t sbits = *reinterpret_cast<const uint16_t*>(
                     rowp + ((((o >> 4) ^ (k & 7)) << 4) | (o & 15)));
                 const float sc = __uint_as_float((uint32_t)sbits << 16);
-                *reinterpret_cast<__half*>(pb + blk * p.nh * 32 + kmajor_off(h, k)) = __float2half_rn(pv4[i] * sc);
+                // tokens past the sequence get P = 0 whatever their stale scale bytes hold
+                *reinterpret_cast<__half*>(pb + blk * p.nh * 32 + kmajor_off(h, k)) =
+                    __float2half_rn(t0 + k < L ? pv4[i] * sc : 0.f);
               }
             }
           } else {
@@ -358,68 +402,50 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
           }
         }
         if (QUANT) {
-          // Dequantize this page's V nibbles into MN-major f16 A tiles. Task = (M-tile,
-          // token, 16-byte window = 32 channels). A window starts at a block-constant
-          // misalignment inside the staged row, so it is cut from two aligned 16-byte
-          // chunks with funnel shifts; 8 nibbles -> 4 half2 with the 0x6400 bias trick.
-          uint8_t* ab = st + LY.v_bytes;
-          const int nvq = p.v_boxes * 8 - 1;    // last staged 16-byte chunk index
-          for (int task = wt; task < nmt * 64; task += kWorkerThreads) {
-            const int m = task >> 6, tt = task & 63;
-            const int k = tt & 15, j = tt >> 4;
-            const int gm = mt0 + m;
-            const bool outl = gm < p.t_out;
-            const int jt = outl ? gm : gm - p.t_out;
-            const int bb = (outl ? p.vq_off : p.vq_off + p.v_nbo) - p.vx0;   // block start in the staged row
-            const int win = bb + 64 * jt + 16 * j;
-            const int c0 = min(win >> 4, nvq), c1 = min((win >> 4) + 1, nvq);
-            const uint8_t* rowp = st + k * 128;
-            const uint4 A0 = *reinterpret_cast<const uint4*>(rowp + (c0 >> 3) * 2048 + (((c0 & 7) ^ (k & 7)) << 4));
-            const uint4 A1 = *reinterpret_cast<const uint4*>(rowp + (c1 >> 3) * 2048 + (((c1 & 7) ^ (k & 7)) << 4));
+          // Dequantize: per task 32 nibbles -> 4 x 8 f16 values n - 8 (channels 0,2,4,6
+          // of each group of 8) or 16 (n - 8) (channels 1,3,5,7), pairs (e, e + 4) per
+          // 32-bit word in the order e0 e4 e1 e5 e2 e6 e3 e7. Channels past a block's end
+          // get values too; their accumulator rows are never flushed.
+          const __half2 bias1 = __float2half2_rn(1032.f), bias16 = __float2half2_rn(1152.f);
+          auto unbias = [](uint32_t bits, __half2 bias) -> uint32_t {
+            const __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&bits), bias);
+            return *reinterpret_cast<const uint32_t*>(&v);
+          };
+#pragma unroll
+          for (int i = 0; i < kMaxDq; ++i) {
+            if (i >= ndq) break;
+            const uint4 A0 = *reinterpret_cast<const uint4*>(st + dq_src0[i]);
+            const uint4 A1 = *reinterpret_cast<const uint4*>(st + dq_src1[i]);
             const uint32_t W8[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
-            const int sh = (bb & 3) * 8;
+            const int sh = dq_sh[i] & 31, wsel = dq_sh[i] >> 5;
             uint32_t w[4];
-            switch ((bb >> 2) & 3) {
+            switch (wsel) {
               case 0:
 #pragma unroll
-                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i], W8[i + 1], sh);
+                for (int q4 = 0; q4 < 4; ++q4) w[q4] = __funnelshift_r(W8[q4], W8[q4 + 1], sh);
                 break;
               case 1:
 #pragma unroll
-                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i + 1], W8[i + 2], sh);
+                for (int q4 = 0; q4 < 4; ++q4) w[q4] = __funnelshift_r(W8[q4 + 1], W8[q4 + 2], sh);
                 break;
               case 2:
 #pragma unroll
-                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i + 2], W8[i + 3], sh);
+                for (int q4 = 0; q4 < 4; ++q4) w[q4] = __funnelshift_r(W8[q4 + 2], W8[q4 + 3], sh);
                 break;
               default:
 #pragma unroll
-                for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(W8[i + 3], W8[i + 4], sh);
+                for (int q4 = 0; q4 < 4; ++q4) w[q4] = __funnelshift_r(W8[q4 + 3], W8[q4 + 4], sh);
                 break;
             }
-            const int ch_first = (outl ? 0 : p.v_nout) + 128 * jt + 32 * j;   // channel of nibble 0
-            const int ch_end = outl ? p.v_nout : p.v_rank;
+            uint8_t* dst = st + dq_dst[i];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              // half2 pairs (e0,e4) (e1,e5) (e2,e6) (e3,e7) of this word's 8 channels
-              uint32_t hv[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const uint32_t bits = ((w[i] >> (4 * e)) & 0x000F000Fu) | 0x64006400u;   // 1024 + n
-                const __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&bits), __float2half2_rn(1032.f));
-                hv[e] = *reinterpret_cast<const uint32_t*>(&hb);
-              }
-              const int cg0 = ch_first + 8 * i;
-              if (cg0 + 8 > ch_end) {   // block tail: zero channels past the block
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  if (cg0 + e >= ch_end) hv[e] &= 0xFFFF0000u;
-                  if (cg0 + e + 4 >= ch_end) hv[e] &= 0x0000FFFFu;
-                }
-              }
-              const int cg = 4 * j + i;   // channel group within the M-tile
-              *reinterpret_cast<uint4*>(ab + m * 4096 + (k >> 3) * 2048 + cg * 128 + (k & 7) * 16) =
-                  make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const uint32_t hi8 = w[q4] >> 8;
+              *reinterpret_cast<uint4*>(dst + q4 * 128) =
+                  make_uint4(unbias((w[q4] & 0x000F000Fu) | 0x64006400u, bias1),
+                             unbias((w[q4] & 0x00F000F0u) | 0x64006400u, bias16),
+                             unbias((hi8 & 0x000F000Fu) | 0x64006400u, bias1),
+                             unbias((hi8 & 0x00F000F0u) | 0x64006400u, bias16));
             }
           }
         }
@@ -451,6 +477,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
       for (int m = wpair; m < nmt; m += kWorkers / 4) {
         const int gm = mt0 + m;
         int ch, ch_end;
+        const float rscale = QUANT && ((row >> 1) & 1) ? 0.0625f : 1.f;   // 3.2-bit odd channels hold 16 (n - 8)
         if (QUANT) {
           // A rows hold each 8-channel group in the order e0 e4 e1 e5 e2 e6 e3 e7
           const bool outl = gm < p.t_out;
@@ -468,7 +495,8 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int h = c0 + i;
-              if (h < p.num_heads) atomicAdd(pvb + (int64_t)h * p.pv_stride + ch, v[i]);
+              if (h >= p.num_heads) continue;
+              atomicAdd(pvb + (int64_t)h * p.pv_stride + ch, v[i] * rscale);
             }
           }
         }
