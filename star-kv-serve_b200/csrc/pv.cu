@@ -285,6 +285,10 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     const int wt = threadIdx.x - 64;     // 0..kWorkerThreads-1
     const int q = warp & 3;
     const int wpair = (warp - 2) >> 2;   // which of the kWorkers / 4 warps of lane quarter q
+    // P tasks (head, 4 tokens) start at the threads with the fewest dequant tasks: the
+    // last 128 worker threads take P tasks 0..127 (the 4 threads of a head stay in
+    // adjacent lanes)
+    const int pw = (wt + 128) % kWorkerThreads;
     uint32_t it = 0, acc_cnt = 0;
     int u = u_begin;
     SubItem si;
@@ -333,7 +337,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
       float mseq[4], f_cur[4], mt_nt[4];
 #pragma unroll
       for (int tk = 0; tk < 4; ++tk) {
-        const int h = min((wt + kWorkerThreads * tk) >> 2, p.num_heads - 1);
+        const int h = min((pw + kWorkerThreads * tk) >> 2, p.num_heads - 1);
         mseq[tk] = msb[h];
         f_cur[tk] = __expf(mtb[(int64_t)h * p.n_tiles + cur_tile] - mseq[tk]);
         mt_nt[tk] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
@@ -350,7 +354,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
           cur_tile = t0 >> 7;
 #pragma unroll
           for (int tk = 0; tk < 4; ++tk) {
-            const int h = min((wt + kWorkerThreads * tk) >> 2, p.num_heads - 1);
+            const int h = min((pw + kWorkerThreads * tk) >> 2, p.num_heads - 1);
             f_cur[tk] = __expf(mt_nt[tk] - mseq[tk]);
             mt_nt[tk] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
           }
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
         // P rows: thread -> (head, 4 consecutive tokens)
 #pragma unroll
         for (int tk = 0; tk < 4; ++tk) {
-          const int task = wt + kWorkerThreads * tk;
+          const int task = pw + kWorkerThreads * tk;
           if (task >= p.nh * 4) break;
           const int h = task >> 2, kq = task & 3;
           float pv4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -464,7 +468,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
           float v = lsum[tk];
           v += __shfl_xor_sync(0xffffffffu, v, 1);
           v += __shfl_xor_sync(0xffffffffu, v, 2);
-          const int task = wt + kWorkerThreads * tk;
+          const int task = pw + kWorkerThreads * tk;
           const int h = task >> 2;
           if ((task & 3) == 0 && task < p.nh * 4 && h < p.num_heads) atomicAdd(p.l_seq + (int64_t)b * p.num_heads + h, v);
         }
