@@ -281,6 +281,8 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
     pp.vs_off = a->vs_off;
     pp.vx0 = a->vs_off & ~15;
     pp.v_boxes = (a->vq_off + a->v_bytes - pp.vx0 + 127) / 128;
+    pp.v_pitch = code_pitch_bytes(a->vq_off + a->v_bytes - pp.vx0);
+    if (pp.v_pitch > 2048) return STARKV_EINVAL;   // one box row of at most 256 8-byte elements
     pp.t_out = (a->v_nout + 127) / 128;
     pp.n_mtiles = pp.t_out + (a->v_rank - a->v_nout + 127) / 128;
   } else {
@@ -290,10 +292,11 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   if (mtpr * pp.nh > 512) mtpr = 512 / pp.nh;
   for (;;) {
     pp.mt_per_range = mtpr;
-    if (pv_smem_bytes(quant, pp) <= 227 * 1024 && mtpr >= 1) {
+    if (quant) {
+      if (mtpr * 64 <= 3 * 384 && pvq_page_stages(pp) >= 2 && pvq_smem_bytes(pp) <= 227 * 1024) break;
+    } else if (pv_smem_bytes(quant, pp) <= 227 * 1024 && mtpr >= 1) {
       // at least two pipeline stages
-      const int stage = (quant ? pp.v_boxes * 2048 + mtpr * 4096 : mtpr * 4096) + 2 * pp.nh * 32 +
-                        ((a->num_heads * 32 + 127) & ~127);
+      const int stage = mtpr * 4096 + 2 * pp.nh * 32 + ((a->num_heads * 32 + 127) & ~127);
       if (2 * ((stage + 1023) & ~1023) <= 200 * 1024) break;
     }
     if (--mtpr < 1) return STARKV_EINVAL;
@@ -311,7 +314,19 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
     if ((st = make_map(&tm_e, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e16, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
   }
-  if ((st = launch_pv(quant, tm_v, tm_e, pp, dev.sms, stream))) return st;
+  if (quant) {
+    // 3.2-bit: one 8-byte-element box row per token covering the V window
+    CUtensorMap tm_vq;
+    const uint64_t dims[3] = {row_elems * es / 8, (uint64_t)a->block_size, (uint64_t)a->num_blocks};
+    const uint64_t str[2] = {(uint64_t)a->cache_stride[1] * es, (uint64_t)a->cache_stride[0] * es};
+    const uint32_t box[3] = {(uint32_t)pp.v_pitch / 8, 16, 1};
+    if ((st = make_map(&tm_vq, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, a->kv_cache, dims, str, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
+    if ((st = launch_pvq(tm_vq, tm_e, pp, dev.sms, stream))) return st;
+  } else if ((st = launch_pv(quant, tm_v, tm_e, pp, dev.sms, stream))) {
+    return st;
+  }
   if (pev) cudaEventRecord(pev[3], stream);
 
   // ---- lift ----

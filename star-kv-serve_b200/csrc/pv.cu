@@ -26,10 +26,13 @@
 //
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-13 workers (P, dequant,
 // accumulator flush; the three warps of a TMEM lane quarter split the M-tiles).
+#include "pv_common.cuh"
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
 
 namespace starkv {
+
+using namespace pvc;
 
 namespace {
 
@@ -69,57 +72,6 @@ __host__ __device__ inline PvLayout pv_layout(bool quant, const PvParams& p) {
   return L;
 }
 
-__device__ __forceinline__ int find_le(const int* prefix, int n, int v) {
-  int lo = 0, hi = n;
-  while (hi - lo > 1) {
-    int mid = (lo + hi) >> 1;
-    if (prefix[mid] <= v) lo = mid; else hi = mid;
-  }
-  return lo;
-}
-
-// Offset of element (row n, k) in a no-swizzle K-major operand of 16 k-elements.
-__device__ __forceinline__ int kmajor_off(int n, int k) {
-  return (n >> 3) * 256 + (k >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2;
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Sub-item iteration shared by all roles: the CTA's unit range [u, u_end) cut at
-// channel-range and sequence boundaries.
-struct SubItem {
-  int range, b, page0, npages;
-};
-
-__device__ __forceinline__ bool next_sub(int& u, int u_end, int total_pages, const int* pprefix, const int* pbeg,
-                                         int n, SubItem& si) {
-  if (u >= u_end) return false;
-  si.range = u / total_pages;
-  const int pi = u % total_pages;
-  si.b = find_le(pprefix, n, pi);
-  si.page0 = pi - pprefix[si.b] + pbeg[si.b];   // absolute page of the sequence
-  const int seq_end = si.range * total_pages + pprefix[si.b + 1];
-  const int e = min(u_end, seq_end);
-  si.npages = e - u;
-  u = e;
-  return true;
-}
-
 }  // namespace
 
 size_t pv_smem_bytes(bool quant, const PvParams& p) {
@@ -140,18 +92,7 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
   const int S = LY.stages;
 
   if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int b = 0; b < p.n; ++b) {
-      pprefix[b] = acc;
-      const int L = min(max(p.seq_lens[b], 0), p.max_seq_len);
-      // this rank's pages: those of its 256-token tiles [T r / w, T (r+1) / w)
-      const int T = (L + 255) >> 8;
-      const int s0 = (int)((int64_t)T * p.cp_rank / p.cp_world), s1 = (int)((int64_t)T * (p.cp_rank + 1) / p.cp_world);
-      const int pg0 = 16 * s0, pg1 = min(16 * s1, (L + 15) >> 4);
-      pbeg[b] = pg0;
-      acc += max(pg1 - pg0, 0);
-    }
-    pprefix[p.n] = acc;
+    pvc::page_ranges(p, pprefix, pbeg);
     for (int s = 0; s < S; ++s) {
       mbar_init(&ctl->vfull[s], 1);
       mbar_init(&ctl->vempty[s], QUANT ? kWorkers : 1);
