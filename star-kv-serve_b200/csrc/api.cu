@@ -187,14 +187,15 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   const uint64_t row_elems = quant ? (uint64_t)a->row_nbytes : (uint64_t)(a->k_width + a->v_rank);
   if (a->cache_stride[1] < (int64_t)row_elems || a->cache_stride[0] < a->cache_stride[1] * a->block_size)
     return STARKV_EINVAL;
-  // P.V: V code tiles straight from the cache (bf16: 64 channels = 128 B per box,
-  // 128-byte swizzle, the MMA's A layout; 3.2-bit: 128-byte boxes of V bytes).
-  {
+  // P.V (bf16 / f16): V code tiles straight from the cache, 64 channels = 128 B per
+  // box row, 128-byte swizzle (the MMA's A layout). The 3.2-bit map is made below.
+  if (!quant) {
     const uint64_t dims[3] = {row_elems, (uint64_t)a->block_size, (uint64_t)a->num_blocks};
     const uint64_t str[2] = {(uint64_t)a->cache_stride[1] * es, (uint64_t)a->cache_stride[0] * es};
-    const CUtensorMapDataType dt = quant ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
-    const uint32_t box[3] = {quant ? 128u : 64u, 16, 1};
-    if ((st = make_map(&tm_v, dt, 3, a->kv_cache, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint32_t box[3] = {64, 16, 1};
+    if ((st = make_map(&tm_v, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a->kv_cache, dims, str, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
   }
   // Scores: code windows cut from an 8-byte-element view of the cache, unswizzled,
   // with the row pitch the kernel stages them at (an odd multiple of 16 bytes).
@@ -280,7 +281,6 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
     pp.v_nout = a->v_nout; pp.v_nbo = a->v_nbo; pp.v_bytes = a->v_bytes; pp.vq_off = a->vq_off;
     pp.vs_off = a->vs_off;
     pp.vx0 = a->vs_off & ~15;
-    pp.v_boxes = (a->vq_off + a->v_bytes - pp.vx0 + 127) / 128;
     pp.v_pitch = code_pitch_bytes(a->vq_off + a->v_bytes - pp.vx0);
     if (pp.v_pitch > 2048) return STARKV_EINVAL;   // one box row of at most 256 8-byte elements
     pp.t_out = (a->v_nout + 127) / 128;
@@ -293,11 +293,10 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
   for (;;) {
     pp.mt_per_range = mtpr;
     if (quant) {
-      if (mtpr * 64 <= 3 * 384 && pvq_page_stages(pp) >= 2 && pvq_smem_bytes(pp) <= 227 * 1024) break;
-    } else if (pv_smem_bytes(quant, pp) <= 227 * 1024 && mtpr >= 1) {
-      // at least two pipeline stages
-      const int stage = mtpr * 4096 + 2 * pp.nh * 32 + ((a->num_heads * 32 + 127) & ~127);
-      if (2 * ((stage + 1023) & ~1023) <= 200 * 1024) break;
+      if (mtpr * 64 <= pvq_max_dequant_tasks() && pvq_page_stages(pp) >= 2 && pvq_smem_bytes(pp) <= 227 * 1024)
+        break;
+    } else if (pv_page_stages(pp) >= 2 && pv_smem_bytes(pp) <= 227 * 1024) {
+      break;
     }
     if (--mtpr < 1) return STARKV_EINVAL;
   }
@@ -324,7 +323,7 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
     if ((st = launch_pvq(tm_vq, tm_e, pp, dev.sms, stream))) return st;
-  } else if ((st = launch_pv(quant, tm_v, tm_e, pp, dev.sms, stream))) {
+  } else if ((st = launch_pv(tm_v, tm_e, pp, dev.sms, stream))) {
     return st;
   }
   if (pev) cudaEventRecord(pev[3], stream);

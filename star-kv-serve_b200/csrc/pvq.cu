@@ -22,7 +22,10 @@
 // dequant tasks (M-tile, token, 32-channel window) are the same on every page, so
 // their addresses are worked out once per page range.
 //
-// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-13 workers.
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-13 workers, 14 second MMA
+// issuer (each issuer takes half of a page's M-tiles: one thread issues an N = 32
+// MMA no faster than every ~50 cycles, so one issuer alone cannot keep up with a
+// page's 13 tiles).
 #include "pv_common.cuh"
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
@@ -37,9 +40,11 @@ constexpr int kMaxVStages = 8;
 constexpr int kAStages = 2;
 constexpr int kWorkers = 12;                 // worker warps (3 per TMEM lane quarter)
 constexpr int kWorkerThreads = 32 * kWorkers;
-constexpr int kThreads = 64 + kWorkerThreads;
+constexpr int kIssuer2 = 2 + kWorkers;       // warp index of the second MMA issuer
+constexpr int kThreads = 32 * (kIssuer2 + 1);
 constexpr int kSmemBudget = 224 * 1024;
 constexpr int kMaxDq = 3;                    // dequant tasks per thread and page (M-tiles <= 18)
+constexpr int kMaxP = 3;                     // P tasks (head, token pair) per thread and page (heads <= 144)
 
 struct Ctl {
   uint64_t vfull[kMaxVStages], vempty[kMaxVStages];
@@ -73,6 +78,8 @@ __host__ __device__ inline Layout layout(const PvParams& p) {
 
 }  // namespace
 
+int pvq_max_dequant_tasks() { return kMaxDq * kWorkerThreads; }
+
 size_t pvq_smem_bytes(const PvParams& p) { return (size_t)layout(p).total; }
 int pvq_page_stages(const PvParams& p) { return layout(p).sv; }
 
@@ -98,9 +105,9 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&ctl->afull[s], kWorkers);
-      mbar_init(&ctl->aempty[s], 1);
+      mbar_init(&ctl->aempty[s], 2);   // one commit per issuer
     }
-    mbar_init(&ctl->accfull, 1);
+    mbar_init(&ctl->accfull, 2);
     mbar_init(&ctl->accempty, kWorkers);
     ctl->abort_flag = 0;
     fence_barrier_init();
@@ -169,9 +176,10 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
         }
       }
     }
-  } else if (warp == 1) {
-    // ================= MMA issuer =================
+  } else if (warp == 1 || warp == kIssuer2) {
+    // ================= MMA issuers: warp 1 the first half of the M-tiles, the other the rest =================
     if (lane == 0) {
+      const bool second = warp == kIssuer2;
       const uint32_t idesc = instr_desc_f16(/*f16*/ 0, /*A MN-major*/ 1, /*B K-major*/ 0, 128, p.nh);
       uint32_t it = 0, acc_cnt = 0;
       int u = u_begin;
@@ -187,12 +195,24 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
           tc_fence_after();
           const uint32_t st = smem_u32(a_ring + s * LY.a_stage);
           const uint32_t pbase = st + LY.a_tiles;
-          for (int m = 0; m < nmt; ++m) {
-            const uint64_t da = smem_desc(st + m * 4096, 2048, 128, kSwizzleNone);   // 8 ch x 8 tok cores
-            const int blk = (mt0 + m) < p.t_out ? 0 : 1;
-            const uint64_t db = smem_desc(pbase + blk * p.nh * 32, 128, 256, kSwizzleNone);
-            umma_f16(tmem + m * p.nh, da, db, idesc, pg > 0);
+          // A tiles are 4 KB apart (descriptor address field in 16-byte units); the
+          // outlier tiles take the first block's P, the rest the second's. Issued in
+          // unrolled groups of 4: a loop branch after every MMA costs ~3x its issue time.
+          // Each issuer commits its own MMAs; the stage is free after both commits.
+          const uint64_t da0 = smem_desc(st, 2048, 128, kSwizzleNone);   // 8 ch x 8 tok cores
+          const uint64_t db_out = smem_desc(pbase, 128, 256, kSwizzleNone);
+          const uint64_t db_in = smem_desc(pbase + p.nh * 32, 128, 256, kSwizzleNone);
+          const uint32_t acc = pg > 0 ? 1u : 0u;
+          const int mh = (nmt + 1) >> 1, mhi = second ? nmt : mh;
+          int m = second ? mh : 0;
+          for (; m + 4 <= mhi; m += 4) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              umma_f16(tmem + (m + i) * p.nh, da0 + (uint64_t)((m + i) * 256), mt0 + m + i < p.t_out ? db_out : db_in,
+                       idesc, acc);
           }
+          for (; m < mhi; ++m)
+            umma_f16(tmem + m * p.nh, da0 + (uint64_t)(m * 256), mt0 + m < p.t_out ? db_out : db_in, idesc, acc);
           umma_commit(&ctl->aempty[s]);
         }
         umma_commit(&ctl->accfull);
@@ -204,8 +224,10 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
     const int wt = threadIdx.x - 64;     // 0..kWorkerThreads-1
     const int q = warp & 3;
     const int wpair = (warp - 2) >> 2;   // which of the kWorkers / 4 warps of lane quarter q
-    // P tasks (head, 4 tokens) start at the threads with the fewest dequant tasks
-    const int pw = (wt + 128) % kWorkerThreads;
+    // P tasks (head, token pair), pt = head * 8 + pair, start at worker thread 64: the
+    // first 64 threads carry the third dequant task. The 8 tasks of a head sit in 8
+    // adjacent lanes.
+    const int pbase = (wt + kWorkerThreads - 64) % kWorkerThreads;
     uint32_t it = 0, acc_cnt = 0;
     int u = u_begin;
     SubItem si;
@@ -217,18 +239,19 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
       const int nmt = min(mt0 + p.mt_per_range, p.n_mtiles) - mt0;
       const float* mtb = p.m_tile + (int64_t)b * p.num_heads * p.n_tiles;
       const float* msb = p.m_seq + (int64_t)b * p.num_heads;
-      float lsum[4] = {0.f, 0.f, 0.f, 0.f};   // sum of P of this thread's (head, 4-token) tasks
+      float lsum[kMaxP];   // sum of P (before the row scale) of this thread's tasks
       // P = e16 * exp(m_tile - m_seq): the factor of the current 128-token tile, and
       // the next tile's max loaded as soon as the current tile starts
       int cur_tile = (si.page0 * 16) >> 7;
       const int last_tile = ((si.page0 + si.npages - 1) * 16) >> 7;
-      float mseq[4], f_cur[4], mt_nt[4];
+      float mseq[kMaxP], f_cur[kMaxP], mt_nt[kMaxP];
 #pragma unroll
-      for (int tk = 0; tk < 4; ++tk) {
-        const int h = min((pw + kWorkerThreads * tk) >> 2, p.num_heads - 1);
-        mseq[tk] = msb[h];
-        f_cur[tk] = __expf(mtb[(int64_t)h * p.n_tiles + cur_tile] - mseq[tk]);
-        mt_nt[tk] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
+      for (int j = 0; j < kMaxP; ++j) {
+        const int h = min((pbase + kWorkerThreads * j) >> 3, p.num_heads - 1);
+        lsum[j] = 0.f;
+        mseq[j] = msb[h];
+        f_cur[j] = __expf(mtb[(int64_t)h * p.n_tiles + cur_tile] - mseq[j]);
+        mt_nt[j] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
       }
       // this thread's dequant tasks: (M-tile, token, 16-byte window = 32 channels) ->
       // source offset in the staged row (the two 16-byte chunks the window spans),
@@ -263,52 +286,55 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
       };
       for (int pg = 0; pg < si.npages; ++pg, ++it) {
         const int sv = it % SV, sa = it % kAStages;
-        if (!mbar_wait(&ctl->aempty[sa], ((it / kAStages) & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+        // the page's rows first: the loads of all dequant tasks are in flight while
+        // this thread waits for its A stage to be released by the MMA
         if (!mbar_wait(&ctl->vfull[sv], (it / SV) & 1, abort_flag, p.status)) { ok = false; break; }
         const uint8_t* vs = v_ring + sv * LY.v_stage;      // [16 rows][pitch], then e16 [heads][16]
         const uint8_t* es = vs + LY.v_rows;
+        uint4 src0[kMaxDq], src1[kMaxDq];
+#pragma unroll
+        for (int i = 0; i < kMaxDq; ++i) {
+          if (i < ndq) {
+            src0[i] = *reinterpret_cast<const uint4*>(vs + dq_src[i]);
+            src1[i] = *reinterpret_cast<const uint4*>(vs + dq_src1[i]);
+          } else {
+            src0[i] = src1[i] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        if (!mbar_wait(&ctl->aempty[sa], ((it / kAStages) & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
         uint8_t* as = a_ring + sa * LY.a_stage;           // A tiles, then P of the two blocks
         uint8_t* pb = as + LY.a_tiles;
         const int t0 = (si.page0 + pg) * 16;
         if ((t0 >> 7) != cur_tile) {   // entering the next tile (uniform across the CTA)
           cur_tile = t0 >> 7;
 #pragma unroll
-          for (int tk = 0; tk < 4; ++tk) {
-            const int h = min((pw + kWorkerThreads * tk) >> 2, p.num_heads - 1);
-            f_cur[tk] = __expf(mt_nt[tk] - mseq[tk]);
-            mt_nt[tk] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
+          for (int j = 0; j < kMaxP; ++j) {
+            const int h = min((pbase + kWorkerThreads * j) >> 3, p.num_heads - 1);
+            f_cur[j] = __expf(mt_nt[j] - mseq[j]);
+            mt_nt[j] = mtb[(int64_t)h * p.n_tiles + min(cur_tile + 1, last_tile)];
           }
         }
-        // P rows of the two scale blocks: thread -> (head, 4 consecutive tokens)
+        // P of the two scale blocks for (head, tokens k0, k0 + 1): one 4-byte store per
+        // block. Tokens past the sequence get P = 0 whatever their stale bytes hold.
 #pragma unroll
-        for (int tk = 0; tk < 4; ++tk) {
-          const int task = pw + kWorkerThreads * tk;
-          if (task >= p.nh * 4) break;
-          const int h = task >> 2, kq = task & 3;
-          float pv4[4] = {0.f, 0.f, 0.f, 0.f};
-          if (h < p.num_heads) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(es + h * 32 + 8 * kq);
-            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-            const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-            const float f = f_cur[tk];
-            pv4[0] = a.x * f; pv4[1] = a.y * f; pv4[2] = c.x * f; pv4[3] = c.y * f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (t0 + 4 * kq + i >= L) pv4[i] = 0.f;
-            lsum[tk] += (pv4[0] + pv4[1]) + (pv4[2] + pv4[3]);
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int k = 4 * kq + i;
-            // (outlier, inlier) bf16 scales of token k; tokens past the sequence get
-            // P = 0 whatever their stale scale bytes hold
-            const uint32_t sw = *reinterpret_cast<const uint32_t*>(vs + k * p.v_pitch + p.vs_off - p.vx0);
-            const bool in = t0 + k < L;
-            *reinterpret_cast<__half*>(pb + kmajor_off(h, k)) =
-                __float2half_rn(in ? pv4[i] * __uint_as_float(sw << 16) : 0.f);
-            *reinterpret_cast<__half*>(pb + p.nh * 32 + kmajor_off(h, k)) =
-                __float2half_rn(in ? pv4[i] * __uint_as_float(sw & 0xFFFF0000u) : 0.f);
-          }
+        for (int j = 0; j < kMaxP; ++j) {
+          const int pt = pbase + kWorkerThreads * j;
+          if (pt >= p.nh * 8) break;
+          const int h = pt >> 3, k0 = (pt & 7) * 2;
+          const bool in0 = h < p.num_heads && t0 + k0 < L, in1 = h < p.num_heads && t0 + k0 + 1 < L;
+          float2 e = make_float2(0.f, 0.f);
+          if (h < p.num_heads) e = __half22float2(*reinterpret_cast<const __half2*>(es + h * 32 + k0 * 2));
+          const float e0 = in0 ? e.x * f_cur[j] : 0.f, e1 = in1 ? e.y * f_cur[j] : 0.f;
+          lsum[j] += e0 + e1;
+          // (outlier, inlier) bf16 scales of tokens k0 and k0 + 1
+          const uint32_t s0 = *reinterpret_cast<const uint32_t*>(vs + k0 * p.v_pitch + p.vs_off - p.vx0);
+          const uint32_t s1 = *reinterpret_cast<const uint32_t*>(vs + (k0 + 1) * p.v_pitch + p.vs_off - p.vx0);
+          const __half2 po = __floats2half2_rn(in0 ? e0 * __uint_as_float(s0 << 16) : 0.f,
+                                               in1 ? e1 * __uint_as_float(s1 << 16) : 0.f);
+          const __half2 pi = __floats2half2_rn(in0 ? e0 * __uint_as_float(s0 & 0xFFFF0000u) : 0.f,
+                                               in1 ? e1 * __uint_as_float(s1 & 0xFFFF0000u) : 0.f);
+          *reinterpret_cast<__half2*>(pb + kmajor_off(h, k0)) = po;
+          *reinterpret_cast<__half2*>(pb + p.nh * 32 + kmajor_off(h, k0)) = pi;
         }
         // dequant: 32 nibbles -> 4 x 8 f16 (n - 8 or 16 (n - 8)), pairs (e, e + 4) per
         // word in the order e0 e4 e1 e5 e2 e6 e3 e7; channels past a block's end get
@@ -316,8 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
 #pragma unroll
         for (int i = 0; i < kMaxDq; ++i) {
           if (i >= ndq) break;
-          const uint4 A0 = *reinterpret_cast<const uint4*>(vs + dq_src[i]);
-          const uint4 A1 = *reinterpret_cast<const uint4*>(vs + dq_src1[i]);
+          const uint4 A0 = src0[i], A1 = src1[i];
           const uint32_t W8[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
           const int sh = dq_sh[i] & 31;
           uint32_t w[4];
@@ -358,16 +383,17 @@ __global__ void __launch_bounds__(kThreads, 1) pvq_kernel(const __grid_constant_
         }
       }
       if (!ok) break;
-      // softmax denominator: the 4 threads of a head sit in adjacent lanes
+      // softmax denominator: the 8 threads of a head sit in adjacent lanes
       if (si.range == 0) {
 #pragma unroll
-        for (int tk = 0; tk < 4; ++tk) {
-          float v = lsum[tk];
+        for (int j = 0; j < kMaxP; ++j) {
+          float v = lsum[j];
           v += __shfl_xor_sync(0xffffffffu, v, 1);
           v += __shfl_xor_sync(0xffffffffu, v, 2);
-          const int task = pw + kWorkerThreads * tk;
-          const int h = task >> 2;
-          if ((task & 3) == 0 && task < p.nh * 4 && h < p.num_heads)
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          const int pt = pbase + kWorkerThreads * j;
+          const int h = pt >> 3;
+          if ((pt & 7) == 0 && pt < p.nh * 8 && h < p.num_heads)
             atomicAdd(p.l_seq + (int64_t)b * p.num_heads + h, v);
         }
       }
@@ -418,6 +444,7 @@ int launch_pvq(const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams&
   if (L.sv < 2) return STARKV_EINVAL;
   if (L.total > 227 * 1024) return STARKV_EINVAL;
   if (p.mt_per_range * 64 > kMaxDq * kWorkerThreads) return STARKV_EINVAL;   // dequant tasks per thread
+  if (p.nh * 8 > kMaxP * kWorkerThreads) return STARKV_EINVAL;               // P tasks per thread
   if (cudaFuncSetAttribute(pvq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) != cudaSuccess)
     return STARKV_ECUDA;
   pvq_kernel<<<num_sms, kThreads, L.total, stream>>>(tm_v, tm_e, p);

@@ -63,7 +63,7 @@ struct PvParams {
   int n_ranges;
   int cache_dtype;
   // 3.2-bit V layout (paged_quant.QuantRow)
-  int v_nout, v_nbo, v_bytes, vq_off, vs_off, vx0, v_boxes;
+  int v_nout, v_nbo, v_bytes, vq_off, vs_off, vx0;
   int v_pitch;            // 3.2-bit: staged row pitch of the V window [vx0, vq_off + v_bytes), odd x 16 B
   int cp_rank, cp_world;  // context split, as in ScoresParams (pages of the rank's 256-token tiles)
   int t_out;              // tiles over the outlier block (the rest cover inliers)
@@ -110,17 +110,18 @@ struct FoldParams {
 size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch);
 int code_pitch_bytes(int bytes);
 int scores_window_bytes(bool quant);
-size_t pv_smem_bytes(bool quant, const PvParams& p);
+size_t pv_smem_bytes(const PvParams& p);
+int pv_page_stages(const PvParams& p);
 size_t pvq_smem_bytes(const PvParams& p);
 int pvq_page_stages(const PvParams& p);
+int pvq_max_dequant_tasks();
 int launch_pvq(const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms, cudaStream_t stream);
 
 int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream);
 int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
                   const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
                   cudaStream_t stream);
-int launch_pv(bool quant, const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms,
-              cudaStream_t stream);
+int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms, cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
 
 }  // namespace starkv
