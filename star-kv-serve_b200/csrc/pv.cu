@@ -19,7 +19,9 @@
 // accumulator with f32 atomics into the small L2-resident pv buffer.
 //
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-13 workers (P, accumulator
-// flush; the three warps of a TMEM lane quarter split the M-tiles).
+// flush; the three warps of a TMEM lane quarter split the M-tiles), 14 second MMA
+// issuer (each issuer takes half of a page's M-tiles: one thread issues an N = 32
+// MMA no faster than every ~50 cycles).
 #include "pv_common.cuh"
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
@@ -33,7 +35,8 @@ namespace {
 constexpr int kMaxStages = 4;
 constexpr int kWorkers = 12;                 // worker warps (3 per TMEM lane quarter)
 constexpr int kWorkerThreads = 32 * kWorkers;
-constexpr int kPvThreads = 64 + kWorkerThreads;
+constexpr int kIssuer2 = 2 + kWorkers;       // warp index of the second MMA issuer
+constexpr int kPvThreads = 32 * (kIssuer2 + 1);
 
 struct PvCtl {
   uint64_t vfull[kMaxStages], vempty[kMaxStages];
@@ -88,11 +91,11 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     pvc::page_ranges(p, pprefix, pbeg);
     for (int s = 0; s < S; ++s) {
       mbar_init(&ctl->vfull[s], 1);
-      mbar_init(&ctl->vempty[s], 1);
+      mbar_init(&ctl->vempty[s], 2);   // one commit per issuer
       mbar_init(&ctl->pfull[s], kWorkers);
-      mbar_init(&ctl->pempty[s], 1);
+      mbar_init(&ctl->pempty[s], 2);
     }
-    mbar_init(&ctl->accfull, 1);
+    mbar_init(&ctl->accfull, 2);
     mbar_init(&ctl->accempty, kWorkers);
     ctl->abort_flag = 0;
     fence_barrier_init();
@@ -169,9 +172,10 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
         }
       }
     }
-  } else if (warp == 1) {
-    // ================= MMA issuer =================
+  } else if (warp == 1 || warp == kIssuer2) {
+    // ================= MMA issuers: warp 1 the first half of the M-tiles, the other the rest =================
     if (lane == 0) {
+      const bool second = warp == kIssuer2;
       const uint32_t fmt = p.cache_dtype == STARKV_BF16 ? 1u : 0u;
       const uint32_t idesc = instr_desc_f16(fmt, /*A MN-major*/ 1, /*B K-major*/ 0, 128, p.nh);
       uint32_t it = 0, acc_cnt = 0;
@@ -188,12 +192,18 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
           if (!mbar_wait(&ctl->pfull[s], (it / S) & 1, abort_flag, p.status)) break;
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * LY.stage_bytes);
-          const uint32_t pbase = st + LY.v_bytes + LY.e_bytes;
-          for (int m = 0; m < nmt; ++m) {
-            const uint64_t da = smem_desc(st + m * 4096, 2048, 1024, kSwizzle128B);
-            const uint64_t db = smem_desc(pbase, 128, 256, kSwizzleNone);
-            umma_f16(tmem + m * p.nh, da, db, idesc, pg > 0);
+          // V tiles are 4 KB apart (descriptor address field in 16-byte units); issued
+          // in unrolled groups of 4: a loop branch after every MMA costs ~3x its issue time
+          const uint64_t da0 = smem_desc(st, 2048, 1024, kSwizzle128B);
+          const uint64_t db = smem_desc(st + LY.v_bytes + LY.e_bytes, 128, 256, kSwizzleNone);
+          const uint32_t acc = pg > 0 ? 1u : 0u;
+          const int mh = (nmt + 1) >> 1, mhi = second ? nmt : mh;
+          int m = second ? mh : 0;
+          for (; m + 4 <= mhi; m += 4) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) umma_f16(tmem + (m + i) * p.nh, da0 + (uint64_t)((m + i) * 256), db, idesc, acc);
           }
+          for (; m < mhi; ++m) umma_f16(tmem + m * p.nh, da0 + (uint64_t)(m * 256), db, idesc, acc);
           umma_commit(&ctl->vempty[s]);
           umma_commit(&ctl->pempty[s]);
         }
