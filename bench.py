@@ -126,16 +126,27 @@ def shard_layer_spec(ranks, world, rank):
     return lpt_shard(ranks, world)[rank]
 
 
-def build_layer(quant: bool, world: int, rank: int, device, batch=None, context=None, parallel="context"):
+def build_layer(quant: bool, world: int, rank: int, device, batch=None, context=None, parallel="context",
+                mixed=False):
     from starkv_b200.workload import make_layer, sample_ranks
-    n, L = (64, 16384) if quant else (64, 8192)
-    n, L = batch or n, context or L
-    ranks, rv = sample_ranks(32, 0)
+    if mixed:
+        # config 4: a serving batch of 256 sequences with contexts uniform in
+        # [1024, 32768] and skewed per-head ranks (K 16..128, V 32..128), seeded
+        import numpy as np
+        rng = np.random.default_rng(4)
+        n = batch or 256
+        lens = [int(x) for x in rng.integers(1024, (context or 32768) + 1, size=n)]
+        ranks, rv = sample_ranks(32, 4, skewed=True)
+    else:
+        n, L = (64, 16384) if quant else (64, 8192)
+        n, L = batch or n, context or L
+        lens = [L] * n
+        ranks, rv = sample_ranks(32, 0)
     # context split: every rank holds the whole layer (all heads) and decodes its
     # share of each sequence; head split: each rank holds its heads (LPT)
     heads = list(range(32)) if world == 1 or parallel == "context" else shard_layer_spec(ranks, world, rank)
     local = [ranks[h] for h in heads]
-    layer = make_layer([L] * n, num_heads=len(local), quant=quant, seed=0, device=device, ranks=local, v_rank=rv)
+    layer = make_layer(lens, num_heads=len(local), quant=quant, seed=0, device=device, ranks=local, v_rank=rv)
     return layer, heads
 
 
@@ -338,9 +349,10 @@ def ours(args):
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
     hbm_peak, tf_peak, peak_kind = peaks()
     res = {}
-    cases = {"c2": (False,), "c3": (True,), "both": (False, True)}[args.case]
+    cases = {"c2": (False,), "c3": (True,), "both": (False, True), "c4": (False, True)}[args.case]
     for quant in cases:
-        layer, heads = build_layer(quant, world, rank, device, args.batch, args.context, args.parallel)
+        layer, heads = build_layer(quant, world, rank, device, args.batch, args.context, args.parallel,
+                                   mixed=args.case == "c4")
         cp = (rank, world) if dist_on and args.parallel == "context" else None
         ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on, cp)
         res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
@@ -348,7 +360,22 @@ def ours(args):
                           roof=roofline_for(layer, per_kernel, hbm_peak, cp))
         del layer
         torch.cuda.empty_cache()
-    if rank == 0 and args.case != "both":
+    if rank == 0 and args.case == "c4":
+        # config 4 (mixed lengths, skewed ranks), both formats: one line, no baselines
+        line = {"case": "c4", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "parallelism": ("single" if world == 1 else f"cp{world} (context split)"
+                                if args.parallel == "context" else f"tp{world} (heads, LPT by rank)"),
+                "sequences": res[False]["layer"].n,
+                "tokens": int(sum(res[False]["layer"].seq_lens_host))}
+        for quant, key in ((False, "bf16"), (True, "q32")):
+            r = res[quant]
+            line[key] = {"ms_per_step": round(r["ms"], 4), "value": round(r["layer"].n / (r["ms"] * 1e-3), 1),
+                         "unit": UNIT, "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
+                         "hbm_frac_step": round(r["alg"] / (r["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+                         "k_width": r["layer"].k_width, "v_rank": r["layer"].v_rank,
+                         "kernel_ms": r["roof"]["kernel_ms"], "clocks": r["clocks"]}
+        print(json.dumps(line), flush=True)
+    elif rank == 0 and args.case != "both":
         # single-configuration run (profiling): short line, no baselines
         r = res[cases[0]]
         print(json.dumps({"case": args.case, "batch": r["layer"].n, "context": r["layer"].seq_lens_host[0],
@@ -427,7 +454,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--case", default="both", choices=["both", "c2", "c3"],
+    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
     ap.add_argument("--parallel", default="context", choices=["context", "heads"],
                     help="N > 1: split every sequence's tiles over the GPUs (all heads each), or shard heads")
