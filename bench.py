@@ -278,6 +278,14 @@ def rank_tokens(layer, cp):
     return tot
 
 
+# DRAM traffic / algorithmic bytes of each kernel, from one ncu capture per kernel at
+# batch 16 with the config shapes (dram__bytes_read.sum + dram__bytes_write.sum;
+# profiles/scores_pv_pvq_kernels_batch16.md). Both grow with the tokens processed, so
+# a full launch's traffic is its algorithmic bytes times this ratio.
+TRAFFIC_RATIO = {(False, "scores"): 414.386688 / 364.904448, (False, "pv"): 444.123136 / 402.653184,
+                 (True, "scores"): 277.952256 / 216.006656, (True, "pv"): 283.142400 / 202.637312}
+
+
 def roofline_for(layer, per_kernel, hbm_peak, cp=None):
     """Dominant kernel's algorithmic bytes per launch / its event-timed duration."""
     T = rank_tokens(layer, cp)
@@ -290,8 +298,11 @@ def roofline_for(layer, per_kernel, hbm_peak, cp=None):
     alg = T * per_tok.get(k, 0)
     ms = per_kernel[k]
     achieved = alg / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
+    ratio = TRAFFIC_RATIO.get((layer.quant, names[k]))
     return {"kernel": names[k], "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
-            "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": None,
+            "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+            "traffic": int(alg * ratio) if ratio else None,
+            "traffic_source": "ncu DRAM bytes at batch 16, scaled by tokens per launch" if ratio else None,
             "alg_bytes_per_launch": alg, "ms_per_launch": round(ms, 4),
             "kernel_ms": {nm: round(v, 4) for nm, v in zip(names, per_kernel)}}
 
