@@ -209,7 +209,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       mbar_init(&ctl->tfull[i], 1);
       mbar_init(&ctl->tempty[i], 2 * kEpiWarps);
     }
-    mbar_init(&ctl->epi, 32 * kEpiWarps);
+    mbar_init(&ctl->epi, kEpiWarps);   // one arrival per epilogue warp
     ctl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -367,8 +367,12 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     uint32_t code_it = 0, tb = 0, item_cnt = 0, epi_phase = 0;
     // Bounded barrier among the epilogue threads (a plain bar.sync could wait
     // forever if another epilogue warp left on a timed-out pipeline wait).
+    // One arrival per warp, after __syncwarp (which orders the lanes' shared-memory
+    // writes before lane 0's release): an arrival per thread, 512 on one barrier
+    // word, serialised in the shared-memory unit.
     auto epi_sync = [&]() -> bool {
-      mbar_arrive(&ctl->epi);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->epi);
       return mbar_wait(&ctl->epi, (epi_phase++) & 1, abort_flag, p.status);
     };
     const uint32_t tempty_l = leader_addr(&ctl->tempty[0]);
