@@ -61,7 +61,6 @@ constexpr int kTmemBufs = kTmemCols / kChunk;
 constexpr int kGroups = kChunk / 32;            // 32-lane groups per chunk
 constexpr int kEpiWarps = 4 * kGroups;          // 4 TMEM lane quarters x groups
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kTokPerWarp = kTile / kEpiWarps;  // tokens per warp in the statistics phase
 constexpr int kMaxAbSlots = 3;
 
 template <bool QUANT>
@@ -84,7 +83,7 @@ struct SharedCtl {
 
 // Shared memory carve-up (byte offsets from the 1024-aligned base).
 struct SmemLayout {
-  int cs, ab, codes, code_slot, sc, logits, red, tiles, prefix, sbeg, ctl, total;
+  int cs, ab, codes, code_slot, sc, logits, tiles, prefix, sbeg, ctl, total;
 };
 
 __host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int k_width, int code_pitch,
@@ -98,8 +97,7 @@ __host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int 
   L.code_slot = (kTile * code_pitch + 127) & ~127;
   L.sc = L.codes + kCodeSlots * L.code_slot;
   L.logits = L.sc + (quant ? (kTile * sc_pitch + 127) & ~127 : 0);
-  L.red = L.logits + H * (kTile + 1) * 4;
-  L.tiles = (L.red + kEpiWarps * H * 4 + 15) & ~15;
+  L.tiles = (L.logits + H * (kTile + 1) * 4 + 15) & ~15;
   L.prefix = L.tiles + nc * (kChunk / 16) * 4;
   L.sbeg = L.prefix + (n + 1) * 4;
   L.ctl = (L.sbeg + n * 4 + 15) & ~15;
@@ -146,7 +144,6 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
   const int NC = (p.k_width + kChunk - 1) / kChunk;
   const SmemLayout SL = smem_layout(QUANT, H, p.n, p.k_width, p.code_pitch, p.sc_pitch);
   float* logits = reinterpret_cast<float*>(smem + SL.logits);    // [H][129]
-  float* red_m = reinterpret_cast<float*>(smem + SL.red);        // [warps][H]
   int* tiles = reinterpret_cast<int*>(smem + SL.tiles);           // [NC * 8], -1 past NT
   int* prefix = reinterpret_cast<int*>(smem + SL.prefix);         // [n+1] item prefix over sequences
   int* sbeg = reinterpret_cast<int*>(smem + SL.sbeg);             // [n] first 256-token tile of this rank
@@ -519,43 +516,36 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         if (lane == 0) mbar_arrive(&ctl->sc_empty);
       }
       if (!ok || !epi_sync()) break;
-      if (t0 < L) {
-        // ---- per-head tile max and e16 = exp(logit - max): warp ew owns 8 tokens ----
-        for (int h = lane; h < H; h += 32) {
-          float m = -INFINITY;
+      // ---- per-head tile max, e16 = exp(logit - max), and the logits cleared for the
+      // next tile's atomic flushes: warp ew owns heads ew, ew + 16, ...; lane l tokens
+      // l, l + 32, l + 64, l + 96 (consecutive words: conflict-free) ----
+      for (int h = ew; h < H; h += kEpiWarps) {
+        float* lrow = logits + h * (kTile + 1);
+        float v[4];
+        float m = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < kTokPerWarp; ++i) {
-            const int t = kTokPerWarp * ew + i;
-            if (t0 + t < L) m = fmaxf(m, logits[h * (kTile + 1) + t]);
-          }
-          red_m[ew * H + h] = m;
+        for (int i = 0; i < 4; ++i) {
+          const int t = lane + 32 * i;
+          v[i] = lrow[t];
+          lrow[t] = 0.f;
+          if (t0 + t < L) m = fmaxf(m, v[i]);
         }
-        if (!epi_sync()) break;
-        for (int h = lane; h < H; h += 32) {
-          float m = red_m[h];
-          for (int w2 = 1; w2 < kEpiWarps; ++w2) m = fmaxf(m, red_m[w2 * H + h]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (t0 < L) {
           const int hq = h * p.group + j;
-          __align__(16) __half ev[kTokPerWarp];
+          __half* dst = p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0;
 #pragma unroll
-          for (int i = 0; i < kTokPerWarp; ++i) {
-            const int t = kTokPerWarp * ew + i;
-            float v = 0.f;
-            if (t0 + t < L) v = __expf(logits[h * (kTile + 1) + t] - m);
-            ev[i] = __float2half_rn(v);
+          for (int i = 0; i < 4; ++i) {
+            const int t = lane + 32 * i;
+            dst[t] = __float2half_rn(t0 + t < L ? __expf(v[i] - m) : 0.f);
           }
-          uint4* dst =
-              reinterpret_cast<uint4*>(p.e16 + ((int64_t)b * p.num_heads + hq) * p.l_pad + t0 + kTokPerWarp * ew);
-#pragma unroll
-          for (int i = 0; i < kTokPerWarp / 8; ++i) dst[i] = reinterpret_cast<const uint4*>(ev)[i];
-          if (ew == 0) {
+          if (lane == 0) {
             p.m_tile[((int64_t)b * p.num_heads + hq) * p.n_tiles + tile] = m;
             atomic_max_f32(p.m_seq + (int64_t)b * p.num_heads + hq, m);
           }
         }
-        if (!epi_sync()) break;
       }
-      // clear the logits for the next tile's atomic flushes
-      for (int i = threadIdx.x - 64; i < H * (kTile + 1); i += 32 * kEpiWarps) logits[i] = 0.f;
       if (!epi_sync()) break;
     }
   }
