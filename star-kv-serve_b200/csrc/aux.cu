@@ -164,12 +164,14 @@ int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream) {
 // Per head a [n x rv] x [rv x 128] product on mma.sync m16n8k16 (bf16 in, f32
 // accumulate). The normalised pv row is split into bf16 hi + lo parts (two MMAs)
 // so the product keeps ~16 mantissa bits, well past the reference's bf16 cast
-// (paged_decode.py:225). Block = (head, 32 output columns, 64 sequences); warp w
-// owns sequences [16w, 16w+16); v_up_by_q tiles are staged through shared memory
-// and read with ldmatrix.trans.
+// (paged_decode.py:225). Block = (head, 32 output columns, 32 sequences), four
+// groups of two warps splitting the V channels; warp w of a group owns sequences
+// [16w, 16w+16); v_up_by_q tiles are staged through shared memory and read with
+// ldmatrix.trans. (64 sequences per block left one 512-thread block per SM and the
+// kernel latency-bound.)
 // ---------------------------------------------------------------------------
 
-constexpr int kLiftBT = 64;    // sequences per block
+constexpr int kLiftBT = 32;    // sequences per block
 constexpr int kLiftVT = 64;    // V channels staged per step
 constexpr int kLiftLd = 40;    // staged row stride (elements): 80 B, conflict-free ldmatrix
 
@@ -187,17 +189,18 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
 }
 
 constexpr int kLiftGroups = 4;   // warp groups splitting the V channels of a block
+constexpr int kLiftGT = 64;      // threads per group (kLiftBT / 16 warps)
 constexpr int kLiftPvtFloats = kLiftBT * (kLiftVT + 4);
 constexpr int kLiftGroupBytes = kLiftPvtFloats * 4 + kLiftVT * kLiftLd * 2;
 constexpr int kLiftSmem = kLiftGroups * kLiftGroupBytes + kLiftBT * 4;
 
-template <class TV>
-__global__ void __launch_bounds__(128 * kLiftGroups) lift_kernel(const LiftParams p) {
+template <class TV, bool VEC>
+__global__ void __launch_bounds__(kLiftGT * kLiftGroups) lift_kernel(const LiftParams p) {
   const int h = blockIdx.x;
   const int d0 = blockIdx.y * 32;
   const int b0 = blockIdx.z * kLiftBT;
-  const int grp = threadIdx.x >> 7;             // this group's V steps: grp, grp + 4, ...
-  const int tid = threadIdx.x & 127, warp = tid >> 5, lane = tid & 31;
+  const int grp = threadIdx.x / kLiftGT;        // this group's V steps: grp, grp + 4, ...
+  const int tid = threadIdx.x % kLiftGT, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   extern __shared__ __align__(16) uint8_t lift_smem[];
   float (*pvt)[kLiftVT + 4] = reinterpret_cast<float (*)[kLiftVT + 4]>(lift_smem + grp * kLiftGroupBytes);   // [b][v]
@@ -213,46 +216,73 @@ __global__ void __launch_bounds__(128 * kLiftGroups) lift_kernel(const LiftParam
       inv_l[threadIdx.x] = 1.f;                        // partial (context-parallel) output: unnormalised
     }
   }
-  // per-thread share of one staged step: 8 x float4 of pv, 16 bf16 of v_up
+  // per-thread share of one staged step: 8 x float4 of pv (32 rows x 16), and 2048
+  // v_up elements (64 v x 32 d): 4 x 8 consecutive d (VEC: 16-byte loads) or 32 scalars
+  constexpr int kVu = VEC ? 4 : 32;
   float4 rp[8];
-  TV rv[16];
+  uint4 rvv[VEC ? 4 : 1];
+  TV rv[VEC ? 1 : 32];
   int vnext = 0;
   auto fetch = [&](int v0) {
     vnext = v0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int e = tid + 128 * i;           // 1024 float4 = 64 rows x 16
+      const int e = tid + kLiftGT * i;
       const int bb = e >> 4, vq = (e & 15) * 4;
       const int b = min(b0 + bb, p.n - 1);
       rp[i] = *reinterpret_cast<const float4*>(p.pv + ((int64_t)b * p.num_heads + h) * p.pv_stride + v0 + vq);
     }
+    if constexpr (VEC) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int e = tid + 128 * i;           // 2048 = 64 v x 32 d
-      const int vv = e >> 5, dd = e & 31;
-      const int v = v0 + vv;
-      const int64_t o = (int64_t)h * p.vu_s0 + (int64_t)min(v, p.v_rank - 1) * p.vu_s1 +
-                        (int64_t)min(d0 + dd, p.head_dim - 1) * p.vu_s2;
-      rv[i] = reinterpret_cast<const TV*>(p.v_up)[o];   // raw load; range masked at the stash
+      for (int i = 0; i < kVu; ++i) {
+        const int e = tid + kLiftGT * i;       // 256 = 64 v x 4 runs of 8 d
+        const int v = min(v0 + (e >> 2), p.v_rank - 1);
+        rvv[i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const TV*>(p.v_up) + (int64_t)h * p.vu_s0 +
+                                                 (int64_t)v * p.vu_s1 + d0 + (e & 3) * 8);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVu; ++i) {
+        const int e = tid + kLiftGT * i;       // 2048 = 64 v x 32 d
+        const int vv = e >> 5, dd = e & 31;
+        const int v = v0 + vv;
+        const int64_t o = (int64_t)h * p.vu_s0 + (int64_t)min(v, p.v_rank - 1) * p.vu_s1 +
+                          (int64_t)min(d0 + dd, p.head_dim - 1) * p.vu_s2;
+        rv[i] = reinterpret_cast<const TV*>(p.v_up)[o];   // raw load; range masked at the stash
+      }
     }
   };
   int vbase = 0;   // first V channel of the step held in rv
   auto stash = [&]() {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int e = tid + 128 * i;
+      const int e = tid + kLiftGT * i;
       *reinterpret_cast<float4*>(&pvt[e >> 4][(e & 15) * 4]) = rp[i];
     }
+    if constexpr (VEC) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int e = tid + 128 * i;
-      const int vv = e >> 5, dd = e & 31;
-      const bool in = (vbase + vv < p.v_rank) && (d0 + dd < p.head_dim);
-      vt[vv][dd] = __float2bfloat16_rn(in ? to_f32(rv[i]) : 0.f);
+      for (int i = 0; i < kVu; ++i) {
+        const int e = tid + kLiftGT * i;
+        const int vv = e >> 2, dq = (e & 3) * 8;
+        const bool in = vbase + vv < p.v_rank;
+        const TV* x = reinterpret_cast<const TV*>(&rvv[i]);
+        __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = __float2bfloat16_rn(in ? to_f32(x[k]) : 0.f);
+        *reinterpret_cast<uint4*>(&vt[vv][dq]) = *reinterpret_cast<const uint4*>(o);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVu; ++i) {
+        const int e = tid + kLiftGT * i;
+        const int vv = e >> 5, dd = e & 31;
+        const bool in = (vbase + vv < p.v_rank) && (d0 + dd < p.head_dim);
+        vt[vv][dd] = __float2bfloat16_rn(in ? to_f32(rv[i]) : 0.f);
+      }
     }
   };
-  // named barrier per group (ids 1..4; 128 threads each)
-  auto group_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(grp + 1) : "memory"); };
+  // named barrier per group (ids 1..4)
+  auto group_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(grp + 1), "n"(kLiftGT) : "memory"); };
   const int rA = 16 * warp + g, rB = rA + 8;   // rows within the block's 64 sequences
   float acc[4][4] = {};
   const int vstride = kLiftVT * kLiftGroups;
@@ -298,12 +328,12 @@ __global__ void __launch_bounds__(128 * kLiftGroups) lift_kernel(const LiftParam
   }
   // reduce the groups' partial sums through shared memory (reusing the staging area)
   __syncthreads();
-  float* red = reinterpret_cast<float*>(lift_smem);   // [group - 1][16][128]
+  float* red = reinterpret_cast<float*>(lift_smem);   // [group - 1][16][kLiftGT]
   if (grp > 0) {
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) red[((grp - 1) * 16 + nt * 4 + k) * 128 + tid] = acc[nt][k];
+      for (int k = 0; k < 4; ++k) red[((grp - 1) * 16 + nt * 4 + k) * kLiftGT + tid] = acc[nt][k];
   }
   __syncthreads();
   if (grp > 0) return;
@@ -312,7 +342,7 @@ __global__ void __launch_bounds__(128 * kLiftGroups) lift_kernel(const LiftParam
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) acc[nt][k] += red[(gg * 16 + nt * 4 + k) * 128 + tid];
+      for (int k = 0; k < 4; ++k) acc[nt][k] += red[(gg * 16 + nt * 4 + k) * kLiftGT + tid];
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
     const int d = d0 + nt * 8 + 2 * t;
@@ -329,16 +359,20 @@ __global__ void __launch_bounds__(128 * kLiftGroups) lift_kernel(const LiftParam
 
 int launch_lift(const LiftParams& p, cudaStream_t stream) {
   dim3 grid(p.num_heads, (p.head_dim + 31) / 32, (p.n + kLiftBT - 1) / kLiftBT);
-  int st = STARKV_OK;
-  with_float_type(p.v_up_dtype, [&](auto tv) {
-    auto fn = lift_kernel<decltype(tv)>;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLiftSmem) != cudaSuccess) {
-      st = STARKV_ECUDA;
-      return;
-    }
-    fn<<<grid, 128 * kLiftGroups, kLiftSmem, stream>>>(p);
-  });
-  if (st) return st;
+  // 16-byte v_up loads: 2-byte elements, unit stride along d, every run of 8 aligned
+  const int es = p.v_up_dtype == STARKV_F32 ? 4 : 2;
+  const bool vec = es == 2 && p.vu_s2 == 1 && p.head_dim % 32 == 0 && p.vu_s0 % 8 == 0 && p.vu_s1 % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.v_up) & 15) == 0;
+  const void* fn = p.v_up_dtype == STARKV_BF16 ? (vec ? (const void*)lift_kernel<__nv_bfloat16, true>
+                                                      : (const void*)lift_kernel<__nv_bfloat16, false>)
+                   : p.v_up_dtype == STARKV_F16 ? (vec ? (const void*)lift_kernel<__half, true>
+                                                       : (const void*)lift_kernel<__half, false>)
+                                                : (const void*)lift_kernel<float, false>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLiftSmem) != cudaSuccess)
+    return STARKV_ECUDA;
+  void* args[] = {const_cast<LiftParams*>(&p)};
+  if (cudaLaunchKernel(fn, grid, dim3(kLiftGT * kLiftGroups), args, kLiftSmem, stream) != cudaSuccess)
+    return STARKV_ECUDA;
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 
