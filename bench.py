@@ -10,14 +10,17 @@ reported under "q32". Inputs are seeded synthetic tensors with the configs'
 shapes and distributions (starkv_b200.workload); every step reads a >2 GB cache,
 far larger than the 126 MB L2, so no flush is needed between steps.
 
-N > 1 (torchrun), --parallel context (default): every rank decodes all heads over
-its share of each sequence's 256-token tiles, and the partial results are combined
-exactly with two small NCCL all-reduces inside the step (starkv_b200.context_parallel);
-each GPU reads 1/N of the K and V codes. --parallel heads: heads sharded
-tensor-parallel (LPT on K width), V codes replicated on every rank (the shared
-latent is read by every head), no collective. Either way the step time is the max
-over ranks and `value` counts the batch's decode tokens once (strong scaling: the
-total work is fixed).
+N > 1 (torchrun), --parallel seqs (default): the decode sequences are independent,
+so every GPU decodes its own batch of configuration 2 (64 sequences; global batch
+64 N) with no collective on the path; `value` is the whole job's decode tokens per
+second (weak scaling: the work per GPU is fixed). Two strong-scaling splits of the
+one 64-sequence batch are kept for study: --parallel context, every rank decodes all
+heads over its share of each sequence's 256-token tiles and the partials are
+combined exactly with one NCCL all-gather and a native kernel
+(starkv_b200.context_parallel), each GPU reading 1/N of the K and V codes; and
+--parallel heads, heads sharded tensor-parallel (LPT on K width) with the V codes
+replicated on every rank (the shared latent is read by every head). The step time is
+always the max over ranks.
 
 --impl reference: the reference algorithm's CPU restatement (oracle/), timed on
 this host's cores on a bounded sample of the same workload.
@@ -142,9 +145,10 @@ def build_layer(quant: bool, world: int, rank: int, device, batch=None, context=
         n, L = batch or n, context or L
         lens = [L] * n
         ranks, rv = sample_ranks(32, 0)
-    # context split: every rank holds the whole layer (all heads) and decodes its
-    # share of each sequence; head split: each rank holds its heads (LPT)
-    heads = list(range(32)) if world == 1 or parallel == "context" else shard_layer_spec(ranks, world, rank)
+    # sequence split: every rank holds the whole layer and its own batch; context
+    # split: every rank holds the whole layer (all heads) and decodes its share of
+    # each sequence; head split: each rank holds its heads (LPT)
+    heads = list(range(32)) if world == 1 or parallel != "heads" else shard_layer_spec(ranks, world, rank)
     local = [ranks[h] for h in heads]
     layer = make_layer(lens, num_heads=len(local), quant=quant, seed=0, device=device, ranks=local, v_rank=rv)
     return layer, heads
@@ -365,6 +369,7 @@ def ours(args):
         layer, heads = build_layer(quant, world, rank, device, args.batch, args.context, args.parallel,
                                    mixed=args.case == "c4")
         cp = (rank, world) if dist_on and args.parallel == "context" else None
+        # sequence split (seqs): every rank decodes its own whole batch
         ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on, cp)
         res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
                           d2h=d2h, alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
@@ -374,15 +379,17 @@ def ours(args):
     if rank == 0 and args.case == "c4":
         # config 4 (mixed lengths, skewed ranks), both formats: one line, no baselines
         line = {"case": "c4", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "parallelism": ("single" if world == 1 else f"cp{world} (context split)"
+                "parallelism": ("single" if world == 1 else f"dp{world} (sequences, a batch per GPU)"
+                                if args.parallel == "seqs" else f"cp{world} (context split)"
                                 if args.parallel == "context" else f"tp{world} (heads, LPT by rank)"),
-                "sequences": res[False]["layer"].n,
+                "sequences": res[False]["layer"].n * (world if args.parallel == "seqs" else 1),
                 "tokens": int(sum(res[False]["layer"].seq_lens_host))}
+        reps = world if args.parallel == "seqs" else 1   # batches in the job (one per GPU under seqs)
         for quant, key in ((False, "bf16"), (True, "q32")):
             r = res[quant]
-            line[key] = {"ms_per_step": round(r["ms"], 4), "value": round(r["layer"].n / (r["ms"] * 1e-3), 1),
-                         "unit": UNIT, "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
-                         "hbm_frac_step": round(r["alg"] / (r["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+            line[key] = {"ms_per_step": round(r["ms"], 4), "value": round(reps * r["layer"].n / (r["ms"] * 1e-3), 1),
+                         "unit": UNIT, "hbm_gbs": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
+                         "hbm_frac_step": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
                          "k_width": r["layer"].k_width, "v_rank": r["layer"].v_rank,
                          "kernel_ms": r["roof"]["kernel_ms"], "clocks": r["clocks"]}
         print(json.dumps(line), flush=True)
@@ -395,37 +402,39 @@ def ours(args):
     elif rank == 0:
         b = res[False]
         n = b["layer"].n
+        reps = world if args.parallel == "seqs" else 1   # batches in the job (one per GPU under seqs)
         cpu_rate, cpu_desc = (None, None)
         if world == 1:
             cpu_rate, cpu_desc = cpu_sample_time(False)
         q = res[True]
         line = {
-            "metric": METRIC, "value": round(n / (b["ms"] * 1e-3), 1), "unit": UNIT,
+            "metric": METRIC, "value": round(reps * n / (b["ms"] * 1e-3), 1), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(b["ms"], 4), "us_per_layer": round(b["ms"] * 1e3, 1),
-            "hbm_gbs": round(b["alg"] / (b["ms"] * 1e-3) / 1e9, 1),
-            "hbm_frac_step": round(b["alg"] / (b["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "hbm_gbs": round(reps * b["alg"] / (b["ms"] * 1e-3) / 1e9, 1),
+            "hbm_frac_step": round(reps * b["alg"] / (b["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+            "higher_is_better": True, "scaling": "strong" if world > 1 and args.parallel != "seqs" else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config shapes)",
             "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
                                    "32 heads x 128, page 16, cache write + decode per step",
-                       "batch": 64, "context": 8192,
-                       "heads_per_gpu": 32 if world == 1 or args.parallel == "context" else 32 // world,
-                       "parallelism": ("single" if world == 1 else f"cp{world} (context split, all heads per GPU)"
+                       "batch": 64, "global_batch": 64 * reps, "context": 8192,
+                       "heads_per_gpu": 32 if world == 1 or args.parallel != "heads" else 32 // world,
+                       "parallelism": ("single" if world == 1 else f"dp{world} (sequences: 64 per GPU, no collective)"
+                                       if args.parallel == "seqs" else f"cp{world} (context split, all heads per GPU)"
                                        if args.parallel == "context" else f"tp{world} (heads)"),
                        "l2": "inputs (2.9 GB cache) larger than L2; no flush"},
             "roofline": dict(b["roof"], peak_kind=peak_kind),
-            "e2e": {"value": round(n / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
+            "e2e": {"value": round(reps * n / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": b["h2d"], "d2h_bytes_per_step": b["d2h"],
                     "ms_per_step": round(b["e2e_ms"], 4)},
             "gpu_launches": (5 if world == 1 or args.parallel != "context" or rank == world - 1 else 4) * args.steps,
             "clocks": b["clocks"],
             "q32": {"workload": "config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
-                    "value": round(q["layer"].n / (q["ms"] * 1e-3), 1), "unit": UNIT, "ms_per_step": round(q["ms"], 4),
-                    "us_per_layer": round(q["ms"] * 1e3, 1),
-                    "hbm_gbs": round(q["alg"] / (q["ms"] * 1e-3) / 1e9, 1),
-                    "hbm_frac_step": round(q["alg"] / (q["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
-                    "tflops": round(q["flops"] / (q["ms"] * 1e-3) / 1e12, 1),
+                    "value": round(reps * q["layer"].n / (q["ms"] * 1e-3), 1), "unit": UNIT,
+                    "ms_per_step": round(q["ms"], 4), "us_per_layer": round(q["ms"] * 1e3, 1),
+                    "hbm_gbs": round(reps * q["alg"] / (q["ms"] * 1e-3) / 1e9, 1),
+                    "hbm_frac_step": round(reps * q["alg"] / (q["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+                    "tflops": round(reps * q["flops"] / (q["ms"] * 1e-3) / 1e12, 1),
                     "roofline": dict(q["roof"], peak_kind=peak_kind),
                     "e2e_ms_per_step": round(q["e2e_ms"], 4), "clocks": q["clocks"]},
         }
@@ -467,8 +476,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
-    ap.add_argument("--parallel", default="context", choices=["context", "heads"],
-                    help="N > 1: split every sequence's tiles over the GPUs (all heads each), or shard heads")
+    ap.add_argument("--parallel", default="seqs", choices=["seqs", "context", "heads"],
+                    help="N > 1: a batch of sequences per GPU (weak scaling, default); or one batch split over "
+                         "the GPUs by each sequence's tiles (context) or by heads")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling small cases)")
     ap.add_argument("--context", type=int, default=None, help="override the context (profiling small cases)")
     a = ap.parse_args()
