@@ -35,6 +35,7 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+CLOCKS_DIR = os.environ.get("STARKV_CLOCKS_DIR", os.path.join(ROOT, "gpurun_out"))
 sys.path.insert(0, os.path.join(ROOT, "star-kv-serve_b200"))
 
 METRIC = "low-rank paged decode attn µs/layer & HBM GB/s; decode tok/s at 1/2/4/8 B200"
@@ -54,7 +55,7 @@ class Clocks:
     """SM clock and clock-event reasons sampled through NVML by a thread, every
     millisecond, for as long as the timed region runs (the region is tens of
     milliseconds, shorter than nvidia-smi's start-up). Samples are also written to
-    gpurun_out/clocks_gpu<i>.csv as a record."""
+    clocks_gpu<i>.csv in the run's output folder (CLOCKS_DIR) as a record."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
@@ -62,7 +63,7 @@ class Clocks:
     def __init__(self, device):
         import threading
         self.samples, self.err = [], None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{device.index or 0}.csv")
+        self.path = os.path.join(CLOCKS_DIR, f"clocks_gpu{device.index or 0}.csv")
         try:
             import pynvml as N
             N.nvmlInit()
