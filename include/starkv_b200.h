@@ -150,6 +150,15 @@ STARKV_API int starkv_paged_decode_q32_partial(const StarKVDecodeArgs* args, int
                                                void* stream);
 
 /*
+ * Self-test of the kernels' bounded pipeline waits (no counterpart in the
+ * reference): one thread waits on a barrier that nothing completes. The wait gives
+ * up after its poll limit (about a second) and records STARKV_ETIMEOUT in the
+ * device status word `status` (caller-zeroed int32), as every pipeline wait in
+ * the decode kernels does instead of hanging.
+ */
+STARKV_API int starkv_selftest_wait_timeout(int32_t* status, void* stream);
+
+/*
  * Combine of context-parallel partials (no counterpart in the reference):
  * parts holds `world` packed partials one after the other, each
  *   out f32 [n, H, 128] | m f32 [n, H] | l f32 [n, H]   (n*H*130 floats)

@@ -567,3 +567,28 @@ extern "C" int starkv_cp_combine(const float* parts, int32_t world, int32_t n, i
                                                                      out_stride[1], out_stride[2], out_dtype);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded pipeline wait: one thread waits on an mbarrier that
+// nothing arrives on; the wait must give up after its poll limit, record
+// STARKV_ETIMEOUT in the status word and return, leaving the context usable.
+// ---------------------------------------------------------------------------
+namespace starkv {
+__global__ void wait_timeout_kernel(int32_t* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && mbar_wait(&bar, 0, &abort_flag, status)) record_status(status, STARKV_EINVAL);
+}
+}  // namespace starkv
+
+extern "C" int starkv_selftest_wait_timeout(int32_t* status, void* stream) {
+  if (!status) return STARKV_EINVAL;
+  starkv::wait_timeout_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(status);
+  return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
+}
