@@ -271,6 +271,67 @@ def measure(layer, device, steps, warmup, dist_on, cp=None):
     return ms, per_kernel, clocks, e2e_ms, h2d, d2h
 
 
+def layer_case(args, device, world, rank, dist_on):
+    """One whole compressed attention layer per step (starkv_b200.layer): Q / kv_down
+    / o_proj GEMMs, rotary, cache write or pack, paged decode; hidden 4096, 32 heads,
+    config 2 (bf16) and config 3 (3.2-bit) caches. N > 1: heads sharded (LPT) with the
+    o_proj all-reduce, or (seqs) a batch per GPU."""
+    import torch
+    import torch.distributed as dist
+    from starkv_b200 import layer as Ly
+    from starkv_b200 import workspace
+    from starkv_b200.workload import make_layer, rope_cos_sin, sample_ranks
+    tp = world if dist_on and args.parallel == "heads" else 1
+    out = {}
+    for quant in (False, True):
+        n, L = (64, 16384) if quant else (64, 8192)
+        n, L = args.batch or n, args.context or L
+        ranks, rv = sample_ranks(32, 0)
+        w = Ly.random_weights(4096, 32, ranks, rv, seed=0, device=device)
+        ly = Ly.StarKVAttentionLayer(w, rope_cos_sin(L, device), quant=quant, rank=rank if tp > 1 else 0,
+                                     world=tp)
+        del w
+        cl = make_layer([L] * n, num_heads=ly.num_heads, quant=quant, seed=0, device=device,
+                        ranks=ly.k_ranks_host, v_rank=rv)
+        g = torch.Generator(device=device).manual_seed(7)
+        hidden = torch.randn(n, 4096, generator=g, device=device).to(torch.bfloat16)
+        pos = torch.full((n,), L - 1, device=device)
+        slots = cl.block_table[torch.arange(n, device=device), pos // 16].long() * 16 + pos % 16
+        ws = workspace.reserve(device, n, ly.num_heads, ly.num_kv_heads, ly.k_width, rv, cl.max_seq_len)
+
+        def fn():
+            return ly.forward(hidden, pos, cl.kv_cache, cl.block_table, cl.seq_lens, cl.max_seq_len, slots, ws=ws)
+
+        for _ in range(args.warmup):
+            fn()
+        if dist_on:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if dist_on:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        reps = world if dist_on and args.parallel == "seqs" else 1
+        out["q32" if quant else "bf16"] = {"us_per_layer": round(ms * 1e3, 1), "ms_per_step": round(ms, 4),
+                                          "value": round(reps * n / (ms * 1e-3), 1), "unit": UNIT,
+                                          "batch": n, "context": L, "heads_per_gpu": ly.num_heads,
+                                          "k_width": ly.k_width, "v_rank": rv}
+        del ly, cl, ws
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps({"case": "layer", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "parallelism": ("single" if world == 1 else f"tp{world} (heads, LPT, o_proj all-reduce)"
+                                          if tp > 1 else f"dp{world} (sequences, a batch per GPU)"),
+                          "hidden": 4096, "heads": 32, **out}), flush=True)
+
+
 def rank_tokens(layer, cp):
     """Tokens this rank decodes: all, or its share of each sequence's 256-token tiles."""
     if cp is None:
@@ -364,6 +425,12 @@ def ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
     hbm_peak, tf_peak, peak_kind = peaks()
+    if args.case == "layer":
+        layer_case(args, device, world, rank, dist_on)
+        if dist_on:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     res = {}
     cases = {"c2": (False,), "c3": (True,), "both": (False, True), "c4": (False, True)}[args.case]
     for quant in cases:
@@ -475,7 +542,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4"],
+    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4", "layer"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
     ap.add_argument("--parallel", default="seqs", choices=["seqs", "context", "heads"],
                     help="N > 1: a batch of sequences per GPU (weak scaling, default); or one batch split over "

@@ -1,0 +1,128 @@
+"""GPU parity of one compressed attention layer's decode step (starkv_b200.layer):
+Q projection + rotary, K/V down-projection to codes, cache write (bf16) or pack
+(3.2-bit), paged decode, o_proj - and its head-sharded tensor-parallel split.
+
+The reference recomputes the attention with the CPU oracle (fp64) from exactly the
+cache rows and rotated queries the GPU produced, then applies o_proj in fp64.
+Tolerance (the target's): 2e-2 abs + 1e-2 rel.
+"""
+import numpy as np
+import pytest
+import torch
+
+import starkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LENS = [1, 40, 300, 1029]
+HIDDEN, HEADS = 512, 8
+
+
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda", 0)
+
+
+def setup(quant, world=1, seed=3):
+    """Weights, one layer per rank, and for each rank a cache holding the codes of
+    every sequence's past tokens (positions 0 .. L-2) computed from seeded hidden
+    states; returns (layers, caches, block_table, seq_lens, hidden_new, positions, slots)."""
+    from starkv_b200 import layer as Ly
+    from starkv_b200.workload import rope_cos_sin, sample_ranks
+    dev = cuda()
+    ranks, rv = sample_ranks(HEADS, seed)
+    w = Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=seed, device=dev)
+    cs = rope_cos_sin(2048, dev)
+    layers = [Ly.StarKVAttentionLayer(w, cs, quant=quant, rank=r, world=world) for r in range(world)]
+    g = torch.Generator(device=dev).manual_seed(seed + 1)
+    npages = [-(-L // 16) for L in LENS]
+    perm = torch.randperm(sum(npages), generator=torch.Generator().manual_seed(seed)) + 1
+    bt = torch.zeros(len(LENS), max(npages), dtype=torch.int32)
+    k = 0
+    for b, p in enumerate(npages):
+        bt[b, :p] = perm[k:k + p]
+        k += p
+    bt = bt.to(dev)
+    caches = []
+    hist = [torch.randn(L, HIDDEN, generator=g, device=dev).to(torch.bfloat16) for L in LENS]
+    for ly in layers:
+        width, dt = ly.cache_row()
+        cache = torch.zeros(sum(npages) + 1, 16, width, dtype=dt, device=dev)
+        for b, L in enumerate(LENS):
+            if L > 1:
+                pos = torch.arange(L - 1, device=dev)
+                slots = bt[b, pos // 16].long() * 16 + pos % 16
+                kc, vc = ly.codes(hist[b][:L - 1])
+                if quant:
+                    from starkv_b200.kernels import paged_quant as pq
+                    pq.pack_kv(kc, vc, cache, slots, ly.row, ly.k_ranks, ly.k_head_offsets, ly.k_nouts)
+                else:
+                    from starkv_b200.kernels.paged_decode import write_kv_bf16
+                    write_kv_bf16(kc, vc, cache, slots)
+        caches.append(cache)
+    new = torch.stack([h[-1] for h in hist])
+    positions = torch.tensor([L - 1 for L in LENS], device=dev)
+    slots = bt[torch.arange(len(LENS), device=dev), positions // 16].long() * 16 + positions % 16
+    seq_lens = torch.tensor(LENS, dtype=torch.int32, device=dev)
+    return layers, caches, bt, seq_lens, new, positions, slots
+
+
+def reference(ly, cache, bt, new, positions):
+    """fp64 oracle attention over the stored cache rows + o_proj."""
+    from starkv_b200.layer import rope
+    f = lambda t: t.double().cpu().numpy()  # noqa: E731
+    q = rope(torch.nn.functional.linear(new, ly.wq).view(len(LENS), ly.num_heads, 128), positions,
+             ly.cos_sin_cache)
+    outs = []
+    row = O.QuantRow(ly.k_width, ly.num_kv_heads, ly.v_rank) if ly.quant else None
+    offs = ly.k_head_offsets.tolist()
+    for b, L in enumerate(LENS):
+        pos = torch.arange(L, device=cache.device)
+        rows = cache[bt[b, pos // 16].long(), pos % 16].cpu()
+        if ly.quant:
+            kd, vd = O.unpack_rows(rows.numpy(), row, ly.k_ranks_host)
+        else:
+            r = rows.double().numpy()
+            kd, vd = r[:, :ly.k_width], r[:, ly.k_width:]
+        outs.append(O.attend_one(f(q[b]), kd, vd, f(ly.k_up), ly.k_ranks_host, offs,
+                                 ly.num_heads // ly.num_kv_heads, f(ly.v_up_by_q), f(ly.cos_sin_cache), ly.scale))
+    attn = np.stack(outs).reshape(len(LENS), -1)
+    return attn @ f(ly.wo).T
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_layer_decode_step_vs_oracle(quant):
+    layers, caches, bt, seq_lens, new, positions, slots = setup(quant)
+    ly, cache = layers[0], caches[0]
+    out = ly.forward(new, positions, cache, bt, seq_lens, max(LENS), slots)
+    assert out.shape == (len(LENS), HIDDEN) and out.dtype == torch.bfloat16
+    # the step's own codes landed in the cache at their slots
+    kc, vc = ly.codes(new)
+    got_rows = cache.view(-1, cache.shape[-1])[slots]
+    if quant:
+        ref_rows = O.pack_rows(kc.float().cpu().numpy(), vc.float().cpu().numpy(),
+                               O.QuantRow(ly.k_width, ly.num_kv_heads, ly.v_rank), ly.k_ranks_host)
+        np.testing.assert_array_equal(got_rows.cpu().numpy(), ref_rows)
+    else:
+        assert torch.equal(got_rows, torch.cat([kc, vc], dim=-1))
+    ref = reference(ly, cache, bt, new, positions)
+    got = out.double().cpu().numpy()
+    err = np.abs(got - ref)
+    assert np.all(err <= 2e-2 + 1e-2 * np.abs(ref)), f"max abs err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_layer_head_shards_sum_to_whole(quant):
+    """Two head shards (LPT) on one GPU: their o_proj partial sums add up to the
+    whole layer's output (the all-reduce of a 2-rank group)."""
+    whole, wc, bt, seq_lens, new, positions, slots = setup(quant, world=1)
+    shards, sc, *_ = setup(quant, world=2)
+    full = whole[0].forward(new, positions, wc[0], bt, seq_lens, max(LENS), slots).float()
+    parts = [ly.forward(new, positions, c, bt, seq_lens, max(LENS), slots, reduce=False).float()
+             for ly, c in zip(shards, sc)]
+    assert sorted(shards[0].heads + shards[1].heads) == list(range(HEADS))
+    got = (parts[0] + parts[1]).cpu().numpy()
+    ref = full.cpu().numpy()
+    err = np.abs(got - ref)
+    assert np.all(err <= 2e-2 + 2e-2 * np.abs(ref)), f"max abs err {err.max():.3e}"
