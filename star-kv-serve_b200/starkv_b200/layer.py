@@ -61,10 +61,12 @@ def random_weights(hidden: int, num_heads: int, ranks: list[int], v_rank: int, s
     for r, o in zip(ranks, offs):
         kv_down[o + r:o + sharding.align16(r)] = 0
         k_up[o:o + r] = rnd(r, HEAD_DIM, std=r ** -0.5)
+    # one V up-projection per KV head, repeated over its query heads (attention.py:158-160)
+    v_up_by_q = rnd(hkv, v_rank, HEAD_DIM, std=v_rank ** -0.5).repeat_interleave(num_heads // hkv, dim=0)
     return AttnWeights(wq=rnd(num_heads * HEAD_DIM, hidden, std=hidden ** -0.5), kv_down=kv_down,
                        wo=rnd(hidden, num_heads * HEAD_DIM, std=(num_heads * HEAD_DIM) ** -0.5), k_up=k_up,
-                       v_up_by_q=rnd(num_heads, v_rank, HEAD_DIM, std=v_rank ** -0.5), k_ranks=list(ranks),
-                       v_rank=v_rank, num_heads=num_heads, num_kv_heads=hkv)
+                       v_up_by_q=v_up_by_q.contiguous(), k_ranks=list(ranks), v_rank=v_rank, num_heads=num_heads,
+                       num_kv_heads=hkv)
 
 
 def rope(x: torch.Tensor, positions: torch.Tensor, cos_sin_cache: torch.Tensor) -> torch.Tensor:
@@ -110,6 +112,19 @@ class StarKVAttentionLayer:
             self._fold_rotations(w.k_ranks, heads, offsets)
         else:
             self.row = None
+        # prefill lifts every head in one bmm over a uniform width: codes gathered
+        # into [T, Hkv, R] (R = the widest head; indices past a head's width repeat
+        # its first lane and meet zero k_up rows), k_up padded to [Hkv, R, Hd]
+        # (attention.py:146-156)
+        R = max(sharding.align16(r) for r in ranks)
+        idx = torch.empty(len(heads) * R, dtype=torch.long)
+        kup = self.k_up.new_zeros(len(heads), R, HEAD_DIM)
+        for i, (r, o) in enumerate(zip(ranks, offsets)):
+            wdt = sharding.align16(r)
+            idx[i * R:i * R + wdt] = torch.arange(o, o + wdt)
+            idx[i * R + wdt:(i + 1) * R] = o
+            kup[i, :wdt] = self.k_up[o:o + wdt]
+        self.k_prefill_gather, self.k_up_T, self.k_max_width = idx.to(dev), kup.contiguous(), R
 
     def _fold_rotations(self, all_ranks: list[int], heads: list[int], offsets: list[int]) -> None:
         """3.2-bit codes are stored in a rotated basis (block Hadamard per K head and
@@ -165,8 +180,45 @@ class StarKVAttentionLayer:
             attn = paged_starkv_decode(q, cache, block_table, seq_lens, max_seq_len, self.k_up, self.k_ranks,
                                        self.k_head_offsets, self.k_width, self.v_up_by_q, self.cos_sin_cache,
                                        self.scale, ws=ws)
-        out = F.linear(attn.reshape(n, -1).to(self.wo.dtype), self.wo)
+        return self._o_proj(attn.reshape(n, -1), reduce)
+
+    def _o_proj(self, attn: torch.Tensor, reduce: bool) -> torch.Tensor:
+        out = F.linear(attn.to(self.wo.dtype), self.wo)
         if self.world > 1 and reduce:
             import torch.distributed as dist
             dist.all_reduce(out, group=self.group)
         return out
+
+    def prefill(self, hidden: torch.Tensor, positions: torch.Tensor, prompt_lens: list[int], cache: torch.Tensor,
+                slot_mapping: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """Dense prefill of whole prompts with nothing cached before them
+        (attention.py:219-251): every prompt token's codes are written / packed at
+        `slot_mapping`, K is lifted per head from this step's own codes with one
+        bmm and rotated, V lifted by v_up, and each prompt attends causally over
+        itself (torch SDPA). hidden [T, hidden] holds the prompts back to back
+        (`prompt_lens`), `positions` their positions; returns o_proj [T, hidden]."""
+        T = hidden.shape[0]
+        if sum(prompt_lens) != T:
+            raise ValueError("prompt_lens must cover the T tokens of hidden")
+        H, G = self.num_kv_heads, self.num_heads // self.num_kv_heads
+        q = rope(F.linear(hidden, self.wq).view(T, self.num_heads, HEAD_DIM), positions, self.cos_sin_cache)
+        kc, vc = self.codes(hidden)
+        if self.quant:
+            pq.pack_kv(kc, vc, cache, slot_mapping, self.row, self.k_ranks, self.k_head_offsets, self.k_nouts)
+        else:
+            write_kv_bf16(kc, vc, cache, slot_mapping)
+        kp = kc[:, self.k_prefill_gather].view(T, H, self.k_max_width)
+        k = rope(torch.bmm(kp.transpose(0, 1), self.k_up_T).transpose(0, 1), positions, self.cos_sin_cache)
+        # V per query head: v_codes . v_up_by_q[hq] (the heads of a KV group share one
+        # v_up in a checkpoint, attention.py:158-160, but nothing here relies on it)
+        v = torch.einsum("tr,hrd->thd", vc, self.v_up_by_q)
+        out = torch.empty(T, self.num_heads, HEAD_DIM, dtype=q.dtype, device=q.device)
+        s0 = 0
+        for L in prompt_lens:
+            qs = q[s0:s0 + L].transpose(0, 1)                                   # [Hq, L, Hd]
+            ks = k[s0:s0 + L].transpose(0, 1).repeat_interleave(G, dim=0)     # [Hq, L, Hd]
+            vs = v[s0:s0 + L].transpose(0, 1)
+            out[s0:s0 + L] = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True,
+                                                            scale=self.scale).transpose(0, 1)
+            s0 += L
+        return self._o_proj(out.reshape(T, -1), reduce)

@@ -126,3 +126,75 @@ def test_layer_head_shards_sum_to_whole(quant):
     ref = full.cpu().numpy()
     err = np.abs(got - ref)
     assert np.all(err <= 2e-2 + 2e-2 * np.abs(ref)), f"max abs err {err.max():.3e}"
+
+
+PROMPTS = [5, 23, 64]
+
+
+def prefill_setup(quant, world=1, seed=11, num_kv_heads=None):
+    from starkv_b200 import layer as Ly
+    from starkv_b200.workload import rope_cos_sin, sample_ranks
+    dev = cuda()
+    hkv = num_kv_heads or HEADS
+    ranks, rv = sample_ranks(hkv, seed)
+    w = Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=seed, num_kv_heads=hkv, device=dev)
+    cs = rope_cos_sin(256, dev)
+    layers = [Ly.StarKVAttentionLayer(w, cs, quant=quant, rank=r, world=world) for r in range(world)]
+    g = torch.Generator(device=dev).manual_seed(seed + 1)
+    T = sum(PROMPTS)
+    hidden = torch.randn(T, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    positions = torch.cat([torch.arange(L, device=dev) for L in PROMPTS])
+    slots = torch.randperm(T + 16, generator=torch.Generator().manual_seed(seed))[:T].to(dev) + 16
+    caches = []
+    for ly in layers:
+        width, dt = ly.cache_row()
+        caches.append(torch.zeros(-(-(T + 32) // 16), 16, width, dtype=dt, device=dev))
+    return layers, caches, hidden, positions, slots
+
+
+def prefill_reference(ly, hidden, positions):
+    """fp64 oracle: each prompt token attends causally over the prompt's own (not
+    quantized) codes, then o_proj."""
+    from starkv_b200.layer import rope
+    f = lambda t: t.double().cpu().numpy()  # noqa: E731
+    T = hidden.shape[0]
+    q = rope(torch.nn.functional.linear(hidden, ly.wq).view(T, ly.num_heads, 128), positions, ly.cos_sin_cache)
+    kc, vc = ly.codes(hidden)
+    kc, vc, qn = f(kc), f(vc), f(q)
+    offs = ly.k_head_offsets.tolist()
+    outs, s0 = [], 0
+    for L in PROMPTS:
+        for t in range(L):
+            outs.append(O.attend_one(qn[s0 + t], kc[s0:s0 + t + 1], vc[s0:s0 + t + 1], f(ly.k_up), ly.k_ranks_host,
+                                     offs, ly.num_heads // ly.num_kv_heads, f(ly.v_up_by_q), f(ly.cos_sin_cache),
+                                     ly.scale))
+        s0 += L
+    return np.stack(outs).reshape(T, -1) @ f(ly.wo).T
+
+
+@pytest.mark.parametrize("quant,hkv", [(False, None), (False, 4), (True, None)])
+def test_layer_prefill_vs_oracle(quant, hkv):
+    layers, caches, hidden, positions, slots = prefill_setup(quant, num_kv_heads=hkv)
+    ly, cache = layers[0], caches[0]
+    out = ly.prefill(hidden, positions, PROMPTS, cache, slots)
+    assert out.shape == (hidden.shape[0], HIDDEN)
+    kc, vc = ly.codes(hidden)
+    got_rows = cache.view(-1, cache.shape[-1])[slots.long()]
+    if quant:
+        ref_rows = O.pack_rows(kc.float().cpu().numpy(), vc.float().cpu().numpy(),
+                               O.QuantRow(ly.k_width, ly.num_kv_heads, ly.v_rank), ly.k_ranks_host)
+        np.testing.assert_array_equal(got_rows.cpu().numpy(), ref_rows)
+    else:
+        assert torch.equal(got_rows, torch.cat([kc, vc], dim=-1))
+    ref = prefill_reference(ly, hidden, positions)
+    err = np.abs(out.double().cpu().numpy() - ref)
+    assert np.all(err <= 2e-2 + 1e-2 * np.abs(ref)), f"max abs err {err.max():.3e}"
+
+
+def test_layer_prefill_head_shards_sum_to_whole():
+    whole, wc, hidden, positions, slots = prefill_setup(False)
+    shards, sc, *_ = prefill_setup(False, world=2)
+    full = whole[0].prefill(hidden, positions, PROMPTS, wc[0], slots).float()
+    parts = [ly.prefill(hidden, positions, PROMPTS, c, slots, reduce=False).float() for ly, c in zip(shards, sc)]
+    err = ((parts[0] + parts[1]) - full).abs()
+    assert bool((err <= 2e-2 + 2e-2 * full.abs()).all()), f"max abs err {err.max().item():.3e}"
