@@ -332,6 +332,85 @@ def layer_case(args, device, world, rank, dist_on):
                           "hidden": 4096, "heads": 32, **out}), flush=True)
 
 
+def model_case(args, device, world, rank, dist_on):
+    """Config 5: decode step of the whole 32-layer Llama-2-7B-geometry model
+    (starkv_b200.model; layers 0, 1, 2, 31 full-rank, the rest STAR-KV at
+    comp-ratio 0.75), `--batch` sessions (default 16) at context `--context`
+    (default 32768), tensor parallel over the N GPUs with the o_proj / down_proj
+    all-reduces; caches filled with synthetic values. The step is captured in a CUDA
+    graph when capture works, else run eagerly."""
+    import torch
+    import torch.distributed as dist
+    from starkv_b200.model import ModelConfig, StarKVModel
+    n, C = args.batch or 16, args.context or 32768
+    cfg = ModelConfig(max_pos=C)
+    model = StarKVModel(cfg, device, quant=False, rank=rank if dist_on else 0, world=world if dist_on else 1,
+                        group=None)
+    pages = -(-C // 16)
+    caches = model.allocate_caches(n * pages + 1)
+    g = torch.Generator(device=device).manual_seed(3)
+    for c in caches:
+        for t in (c if isinstance(c, tuple) else (c,)):
+            t.normal_(0.0, 1.0, generator=g)
+    perm = torch.randperm(n * pages, generator=torch.Generator().manual_seed(1)) + 1
+    bt = perm.view(n, pages).to(device=device, dtype=torch.int32)
+    pos = torch.full((n,), C - 1, device=device)
+    slots = bt[torch.arange(n, device=device), pos // 16].long() * 16 + pos % 16
+    seq_lens = torch.full((n,), C, dtype=torch.int32, device=device)
+    tokens = torch.randint(0, cfg.vocab, (n,), generator=g, device=device)
+
+    def step():
+        return model.decode_step(tokens, pos, caches, bt, seq_lens, C, slots)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    graph, mode = None, "eager"
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        mode = "cuda graph"
+    except Exception as e:   # capture unsupported somewhere: time the eager step
+        graph = None
+        mode = f"eager (capture failed: {type(e).__name__})"
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+    for _ in range(2):
+        run()
+    if dist_on:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist_on:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kv_gb = sum(sum(t.numel() * t.element_size() for t in (c if isinstance(c, tuple) else (c,))) for c in caches) / 1e9
+    if rank == 0:
+        print(json.dumps({"case": "model", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "workload": "config5: 32-layer Llama-2-7B geometry (hidden 4096, FFN 11008, vocab "
+                                      "32000), layers 0,1,2,31 full-rank bf16 KV, 28 STAR-KV bf16 layers",
+                          "sessions": n, "context": C, "parallelism": f"tp{world}" if dist_on else "single",
+                          "mode": mode, "ms_per_step": round(ms, 3), "value": round(n / (ms * 1e-3), 1),
+                          "unit": "decode tok/s (whole model)", "kv_cache_gb_per_gpu": round(kv_gb, 1),
+                          "data": "synthetic (seeded random-init weights and caches)"}), flush=True)
+    del graph, model, caches
+    torch.cuda.empty_cache()
+
+
 def rank_tokens(layer, cp):
     """Tokens this rank decodes: all, or its share of each sequence's 256-token tiles."""
     if cp is None:
@@ -425,8 +504,8 @@ def ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
     hbm_peak, tf_peak, peak_kind = peaks()
-    if args.case == "layer":
-        layer_case(args, device, world, rank, dist_on)
+    if args.case in ("layer", "model"):
+        (layer_case if args.case == "layer" else model_case)(args, device, world, rank, dist_on)
         if dist_on:
             dist.barrier()
             dist.destroy_process_group()
@@ -542,7 +621,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4", "layer"],
+    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4", "layer", "model"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
     ap.add_argument("--parallel", default="seqs", choices=["seqs", "context", "heads"],
                     help="N > 1: a batch of sequences per GPU (weak scaling, default); or one batch split over "
