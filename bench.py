@@ -427,8 +427,8 @@ def rank_tokens(layer, cp):
 # batch 16 with the config shapes (dram__bytes_read.sum + dram__bytes_write.sum;
 # profiles/scores_pv_pvq_kernels_batch16.md). Both grow with the tokens processed, so
 # a full launch's traffic is its algorithmic bytes times this ratio.
-TRAFFIC_RATIO = {(False, "scores"): 414.386688 / 364.904448, (False, "pv"): 444.123136 / 402.653184,
-                 (True, "scores"): 277.952256 / 216.006656, (True, "pv"): 283.142400 / 202.637312}
+TRAFFIC_RATIO = {(False, "scores"): 414.386944 / 364.904448, (False, "pv"): 444.123136 / 402.653184,
+                 (True, "scores"): 280.232960 / 216.006656, (True, "pv"): 283.142400 / 202.637312}
 
 
 def roofline_for(layer, per_kernel, hbm_peak, cp=None):
