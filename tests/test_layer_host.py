@@ -1,0 +1,92 @@
+"""CPU checks of the attention layer's host logic (starkv_b200.layer) and the model
+config: how a tensor-parallel shard slices the weights, and that folding the 3.2-bit
+rotations into the factors leaves every head's K and V products unchanged."""
+import pytest
+import torch
+
+from starkv_b200 import layer as Ly
+from starkv_b200 import sharding
+from starkv_b200.workload import sample_ranks
+
+HIDDEN, HEADS = 256, 8
+
+
+def weights(hkv=None, seed=2):
+    ranks, rv = sample_ranks(hkv or HEADS, seed)
+    return Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=seed, num_kv_heads=hkv, device="cpu",
+                             dtype=torch.float32)
+
+
+@pytest.mark.parametrize("world,hkv", [(2, None), (4, None), (2, 4)])
+def test_shards_partition_heads_and_slice_weights(world, hkv):
+    w = weights(hkv)
+    cs = torch.randn(16, 128)
+    shards = [Ly.StarKVAttentionLayer(w, cs, rank=r, world=world) for r in range(world)]
+    kv_heads = sorted(h for s in shards for h in s.heads)
+    assert kv_heads == list(range(w.num_kv_heads))
+    q_heads = sorted(h for s in shards for h in s.q_heads)
+    assert q_heads == list(range(w.num_heads))
+    W_full = sum(sharding.align16(r) for r in w.k_ranks)
+    for s in shards:
+        qh = torch.tensor(s.q_heads)
+        assert torch.equal(s.wq, w.wq.view(HEADS, 128, HIDDEN)[qh].reshape(-1, HIDDEN))
+        assert torch.equal(s.wo, w.wo.view(HIDDEN, HEADS, 128)[:, qh].reshape(HIDDEN, -1))
+        assert torch.equal(s.v_up_by_q, w.v_up_by_q[qh])
+        _, _, _, lanes = sharding.shard_lanes(w.k_ranks, s.heads)
+        assert torch.equal(s.kv_down[:s.k_width], w.kv_down[torch.tensor(lanes)])
+        assert torch.equal(s.kv_down[s.k_width:], w.kv_down[W_full:])       # V replicated
+        assert torch.equal(s.k_up, w.k_up[torch.tensor(lanes)])
+    # the shards' output columns add up to the whole o_proj
+    whole = Ly.StarKVAttentionLayer(w, cs)
+    x = torch.randn(3, HEADS * 128)
+    parts = sum(x.view(3, HEADS, 128)[:, torch.tensor(s.q_heads)].reshape(3, -1) @ s.wo.t() for s in shards)
+    torch.testing.assert_close(parts, x @ whole.wo.t(), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_folded_rotations_keep_k_and_v_products(world):
+    """3.2-bit layer: codes come out of kv_down rotated, and codes . k_up (per head)
+    and v_codes . v_up_by_q equal the unrotated products."""
+    w = weights()
+    cs = torch.randn(16, 128)
+    h = torch.randn(5, HIDDEN)
+    for r in range(world):
+        plain = Ly.StarKVAttentionLayer(w, cs, quant=False, rank=r, world=world)
+        rot = Ly.StarKVAttentionLayer(w, cs, quant=True, rank=r, world=world)
+        kp, vp = plain.codes(h)
+        kr, vr = rot.codes(h)
+        assert not torch.allclose(kp, kr)                      # the stored basis differs ...
+        for rk, o in zip(plain.k_ranks_host, plain.k_head_offsets.tolist()):
+            torch.testing.assert_close(kr[:, o:o + rk] @ rot.k_up[o:o + rk], kp[:, o:o + rk] @ plain.k_up[o:o + rk],
+                                       rtol=1e-4, atol=1e-4)   # ... the lifted K does not
+        torch.testing.assert_close(torch.einsum("tr,hrd->thd", vr, rot.v_up_by_q),
+                                   torch.einsum("tr,hrd->thd", vp, plain.v_up_by_q), rtol=1e-4, atol=1e-4)
+
+
+def test_shard_rotations_match_whole_layer():
+    """A shard uses the same per-head rotations as the whole layer, so its codes
+    equal the whole layer's codes of its heads."""
+    w = weights()
+    cs = torch.randn(16, 128)
+    h = torch.randn(4, HIDDEN)
+    whole = Ly.StarKVAttentionLayer(w, cs, quant=True)
+    kw, vw = whole.codes(h)
+    for r in range(2):
+        s = Ly.StarKVAttentionLayer(w, cs, quant=True, rank=r, world=2)
+        ks, vs = s.codes(h)
+        _, _, _, lanes = sharding.shard_lanes(w.k_ranks, s.heads)
+        torch.testing.assert_close(ks, kw[:, torch.tensor(lanes)], rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(vs, vw, rtol=1e-5, atol=1e-5)
+
+
+def test_model_config_rank_sampler():
+    from starkv_b200.model import ModelConfig
+    cfg = ModelConfig()
+    Ws, rvs = [], []
+    for i in range(32):
+        ranks, rv = cfg.layer_ranks(i)
+        assert len(ranks) == 32 and all(r in (16, 32, 48) for r in ranks) and rv % 32 == 0
+        Ws.append(sum(sharding.align16(r) for r in ranks))
+        rvs.append(rv)
+    assert 850 < sum(Ws) / 32 < 1150 and 1100 < sum(rvs) / 32 < 1450    # comp-ratio 0.75 sizes
+    assert cfg.layer_ranks(5) == ModelConfig().layer_ranks(5)           # seeded: every rank agrees
