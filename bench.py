@@ -335,19 +335,49 @@ def layer_case(args, device, world, rank, dist_on):
 def model_case(args, device, world, rank, dist_on):
     """Config 5: decode step of the whole 32-layer Llama-2-7B-geometry model
     (starkv_b200.model; layers 0, 1, 2, 31 full-rank, the rest STAR-KV at
-    comp-ratio 0.75), `--batch` sessions (default 16) at context `--context`
-    (default 32768), tensor parallel over the N GPUs with the o_proj / down_proj
-    all-reduces; caches filled with synthetic values. The step is captured in a CUDA
-    graph when capture works, else run eagerly."""
+    comp-ratio 0.75), `--batch` sessions at context `--context` (default 32768),
+    tensor parallel over the N GPUs with the o_proj / down_proj all-reduces; caches
+    filled with synthetic values. Without `--batch` the sessions are as many as fit in
+    85% of the HBM left free after the weights (the configuration's "max concurrency").
+    With `--parallel context` the compressed layers split their caches by pages instead
+    of heads (page p of a sequence on rank p % N; every rank decodes all heads over its
+    pages, and the partials are all-gathered and combined exactly). The step is captured
+    in a CUDA graph when capture works, else run eagerly."""
     import torch
     import torch.distributed as dist
+    from starkv_b200 import context_parallel as cp
     from starkv_b200.model import ModelConfig, StarKVModel
-    n, C = args.batch or 16, args.context or 32768
+    C = args.context or 32768
+    split = "context" if dist_on and args.parallel == "context" else "heads"
     cfg = ModelConfig(max_pos=C)
     model = StarKVModel(cfg, device, quant=False, rank=rank if dist_on else 0, world=world if dist_on else 1,
-                        group=None)
+                        group=None, attn_parallel=split)
+    if args.batch:
+        n = args.batch
+    else:
+        free = torch.cuda.mem_get_info(device)[0]
+        n = max(1, int(0.85 * free / (C * model.kv_bytes_per_token())))
+        if dist_on:   # every rank runs the same sessions
+            t = torch.tensor([n], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            n = int(t.item())
     pages = -(-C // 16)
-    caches = model.allocate_caches(n * pages + 1)
+    local = None
+    if split == "context":
+        # this rank's pages of every sequence, as its own local sequences
+        llen = int(cp.local_len(C, rank, world))
+        lpages = max(-(-llen // 16), 1)
+        lbt = (torch.randperm(n * lpages, generator=torch.Generator().manual_seed(2 + rank)) + 1).view(n, lpages)
+        lbt = lbt.to(device=device, dtype=torch.int32)
+        li = int(cp.local_index(C - 1, world))
+        if int(cp.page_owner(C - 1, world)) == rank:
+            lslots = lbt[:, li // 16].long() * 16 + li % 16
+        else:
+            lslots = torch.full((n,), -1, dtype=torch.long, device=device)
+        local = (lbt, torch.full((n,), llen, dtype=torch.int32, device=device), max(llen, 1), lslots)
+        caches = model.allocate_caches(n * pages + 1, n * lpages + 1)
+    else:
+        caches = model.allocate_caches(n * pages + 1)
     g = torch.Generator(device=device).manual_seed(3)
     for c in caches:
         for t in (c if isinstance(c, tuple) else (c,)):
@@ -360,7 +390,7 @@ def model_case(args, device, world, rank, dist_on):
     tokens = torch.randint(0, cfg.vocab, (n,), generator=g, device=device)
 
     def step():
-        return model.decode_step(tokens, pos, caches, bt, seq_lens, C, slots)
+        return model.decode_step(tokens, pos, caches, bt, seq_lens, C, slots, local=local)
 
     for _ in range(args.warmup):
         step()
@@ -404,6 +434,8 @@ def model_case(args, device, world, rank, dist_on):
                           "workload": "config5: 32-layer Llama-2-7B geometry (hidden 4096, FFN 11008, vocab "
                                       "32000), layers 0,1,2,31 full-rank bf16 KV, 28 STAR-KV bf16 layers",
                           "sessions": n, "context": C, "parallelism": f"tp{world}" if dist_on else "single",
+                          "compressed_attention_split": "pages (context parallel)" if split == "context"
+                          else "heads",
                           "mode": mode, "ms_per_step": round(ms, 3), "value": round(n / (ms * 1e-3), 1),
                           "unit": "decode tok/s (whole model)", "kv_cache_gb_per_gpu": round(kv_gb, 1),
                           "data": "synthetic (seeded random-init weights and caches)"}), flush=True)

@@ -84,3 +84,50 @@ def combine_local(parts: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]], 
     n, H = parts[0][1].shape
     stacked = torch.cat([_packed(*p) for p in parts])
     return _combine_parts(stacked, len(parts), n, H, dtype)
+
+
+# ---------------------------------------------------------------------------
+# Page round-robin placement (growing sequences).
+#
+# The split above divides a sequence whose length is known. A served sequence grows
+# by one token per step, and its tokens must not move between ranks as it grows, so
+# the whole model stores page p of every sequence (tokens 16p .. 16p+15) on rank
+# p % world. On its rank a page is local page p // world, and the rank's pages of a
+# sequence form one contiguous local sequence that the decode kernels read like any
+# other. Only the rotary rows differ: the score kernel takes row i of the table for
+# local token i, so each rank passes a table whose row i holds the rotary row of that
+# token's global position. The keys are then rotated at their true positions, and
+# the partial results combine exactly as above.
+# ---------------------------------------------------------------------------
+
+def page_owner(pos, world: int, block_size: int = 16):
+    """Rank that stores global position `pos` (int or tensor)."""
+    return (pos // block_size) % world
+
+
+def local_index(pos, world: int, block_size: int = 16):
+    """Index of global position `pos` in its owner's local sequence."""
+    return (pos // block_size // world) * block_size + pos % block_size
+
+
+def global_position(i, rank: int, world: int, block_size: int = 16):
+    """Global position of local token `i` of `rank` (the inverse of local_index)."""
+    return ((i // block_size) * world + rank) * block_size + i % block_size
+
+
+def local_len(L, rank: int, world: int, block_size: int = 16):
+    """Tokens of a sequence of length `L` (int or tensor) that `rank` stores."""
+    full, rem = L // block_size, L % block_size
+    n_full = (full - rank + world - 1) // world            # owned whole pages among 0 .. full-1
+    tail = rem * ((full % world) == rank)                 # the partial last page, if owned
+    return n_full * block_size + tail
+
+
+def local_rotary_table(cos_sin_cache: torch.Tensor, rank: int, world: int, block_size: int = 16) -> torch.Tensor:
+    """[ceil(P / world) rounded to pages, 128] table whose row i is row
+    global_position(i) of `cos_sin_cache` ([P, 128]); rows past P repeat its last
+    row and are never read for a sequence shorter than P."""
+    P = cos_sin_cache.shape[0]
+    rows = -(-P // (block_size * world)) * block_size
+    i = torch.arange(rows, device=cos_sin_cache.device)
+    return cos_sin_cache[global_position(i, rank, world, block_size).clamp(max=P - 1)].contiguous()

@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from . import sharding
+from . import context_parallel, sharding
 from .kernels import paged_quant as pq
 from .kernels.paged_decode import paged_starkv_decode, write_kv_bf16
 
@@ -222,3 +222,56 @@ class StarKVAttentionLayer:
                                                             scale=self.scale).transpose(0, 1)
             s0 += L
         return self._o_proj(out.reshape(T, -1), reduce)
+
+
+class StarKVContextLayer(StarKVAttentionLayer):
+    """The layer's decode step with the KV cache split by pages over `world` ranks
+    (context parallel, starkv_b200.context_parallel): page p of every sequence lives on
+    rank p % world. Every rank keeps the whole layer (all heads, the whole o_proj),
+    so K and V codes are both divided by `world`, where head sharding must keep the V
+    latent whole on every rank (checkpoint.py:140-153). Per step each rank writes the
+    codes of the tokens whose page it owns, decodes all heads over its own pages into
+    a partial (out, max, denominator), and the partials are all-gathered and combined
+    exactly; o_proj then runs on every rank with no all-reduce."""
+
+    def __init__(self, w: AttnWeights, cos_sin_cache: torch.Tensor, quant: bool = False, rank: int = 0,
+                 world: int = 1, group=None, block_size: int = 16):
+        super().__init__(w, cos_sin_cache, quant=quant)
+        self.cp_rank, self.cp_world, self.cp_group, self.block_size = rank, world, group, block_size
+        self.local_cos_sin = context_parallel.local_rotary_table(cos_sin_cache, rank, world, block_size)
+
+    def forward_partial(self, hidden: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor,
+                        block_table: torch.Tensor, seq_lens: torch.Tensor, max_seq_len: int,
+                        slot_mapping: torch.Tensor, ws=None):
+        """This rank's part of a decode step. `positions` are global (the query's
+        rotary); `block_table`, `seq_lens` (including the new token where this rank
+        owns its page), `max_seq_len` and `slot_mapping` (-1 where another rank owns
+        the page) describe this rank's local sequences. Returns (out f32 [n, H, 128]
+        unnormalised, m [n, H], l [n, H])."""
+        n = hidden.shape[0]
+        q = rope(F.linear(hidden, self.wq).view(n, self.num_heads, HEAD_DIM), positions, self.cos_sin_cache)
+        k, v = self.codes(hidden)
+        if self.quant:
+            pq.pack_kv(k, v, cache, slot_mapping, self.row, self.k_ranks, self.k_head_offsets, self.k_nouts)
+            return pq.paged_quant_decode(q, cache, block_table, seq_lens, max_seq_len, self.row, self.k_up,
+                                         self.head_of_lane, self.k_tiles, self.v_up_by_q, self.local_cos_sin,
+                                         self.scale, ws=ws, context=(0, 1))
+        write_kv_bf16(k, v, cache, slot_mapping)
+        return paged_starkv_decode(q, cache, block_table, seq_lens, max_seq_len, self.k_up, self.k_ranks,
+                                   self.k_head_offsets, self.k_width, self.v_up_by_q, self.local_cos_sin,
+                                   self.scale, ws=ws, context=(0, 1))
+
+    def forward(self, hidden, positions, cache, block_table, seq_lens, max_seq_len, slot_mapping, ws=None,
+                reduce: bool = True) -> torch.Tensor:
+        """Decode step over this rank's pages, the exchange and combination of the
+        partials, and o_proj: [n, hidden], the same on every rank (`reduce` is
+        accepted for the signature of StarKVAttentionLayer.forward; there is no
+        partial sum to reduce)."""
+        n = hidden.shape[0]
+        out, m, l = self.forward_partial(hidden, positions, cache, block_table, seq_lens, max_seq_len,
+                                         slot_mapping, ws)
+        if self.cp_world > 1:
+            attn = context_parallel.combine(out, m, l, self.cp_group, dtype=self.wo.dtype)
+        else:
+            attn = context_parallel.combine_local([(out, m, l)], dtype=self.wo.dtype)
+        return F.linear(attn.reshape(n, -1), self.wo)

@@ -10,6 +10,12 @@ Megatron layout the reference leaves at TP=1 (model.py:32-33): attention heads a
 the MLP's intermediate columns are split, o_proj and down_proj are row-parallel
 and all-reduced; embedding, norms and LM head are replicated. Weights are
 seeded random-init of the configured geometry.
+
+With attn_parallel="context" the compressed layers split their KV cache by pages
+instead of heads (starkv_b200.layer.StarKVContextLayer): every rank holds all heads
+and 1/world of every sequence's pages, so the V latent, which head sharding keeps
+whole on every rank, is divided too. The full-rank layers and the MLP stay
+tensor parallel.
 """
 from __future__ import annotations
 
@@ -20,7 +26,7 @@ import torch
 import torch.nn.functional as F
 
 from . import sharding
-from .layer import HEAD_DIM, AttnWeights, StarKVAttentionLayer, rope
+from .layer import HEAD_DIM, AttnWeights, StarKVAttentionLayer, StarKVContextLayer, rope
 from .workload import rope_cos_sin
 
 
@@ -109,8 +115,11 @@ class StarKVModel:
     """The model on one rank of a tensor-parallel group (world 1: whole)."""
 
     def __init__(self, cfg: ModelConfig, device, quant: bool = False, rank: int = 0, world: int = 1, group=None,
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, attn_parallel: str = "heads"):
+        if attn_parallel not in ("heads", "context"):
+            raise ValueError(f"attn_parallel must be 'heads' or 'context', not {attn_parallel!r}")
         self.cfg, self.quant, self.rank, self.world, self.group = cfg, quant, rank, world, group
+        self.attn_parallel = attn_parallel
         self.device = torch.device(device)
         d, H = cfg.hidden, cfg.heads
         g = torch.Generator(device=self.device).manual_seed(cfg.seed)
@@ -144,8 +153,12 @@ class StarKVModel:
                 v_up_by_q = _rnd((H, rv, HEAD_DIM), rv ** -0.5, gl, self.device, dtype)
                 w = AttnWeights(wq=wq, kv_down=kv_down, wo=wo, k_up=k_up, v_up_by_q=v_up_by_q, k_ranks=ranks,
                                 v_rank=rv, num_heads=H, num_kv_heads=H)
-                attn = StarKVAttentionLayer(w, self.cos_sin_cache, quant=quant, rank=rank, world=world,
-                                            group=group)
+                if attn_parallel == "context":
+                    attn = StarKVContextLayer(w, self.cos_sin_cache, quant=quant, rank=rank, world=world,
+                                              group=group)
+                else:
+                    attn = StarKVAttentionLayer(w, self.cos_sin_cache, quant=quant, rank=rank, world=world,
+                                                group=group)
                 del w, kv_down, k_up, v_up_by_q
             gate_up = _rnd((2 * cfg.ffn, d), d ** -0.5, gl, self.device, dtype)
             down = _rnd((d, cfg.ffn), cfg.ffn ** -0.5, gl, self.device, dtype)
@@ -157,9 +170,11 @@ class StarKVModel:
             del wq, wo, gate_up, down
         torch.cuda.empty_cache()
 
-    def allocate_caches(self, num_blocks: int) -> list:
-        """One paged cache per layer (16-token blocks): STAR-KV code rows, or the
-        stock (key, value) pair."""
+    def allocate_caches(self, num_blocks: int, compressed_blocks: int | None = None) -> list:
+        """One paged cache per layer (16-token blocks): STAR-KV code rows
+        (`compressed_blocks` of them, default `num_blocks`: with attn_parallel
+        "context" a rank holds only its pages of every sequence), or the stock
+        (key, value) pair."""
         caches = []
         for ly in self.layers:
             a = ly["attn"]
@@ -169,8 +184,22 @@ class StarKVModel:
                                torch.zeros(vs, dtype=torch.bfloat16, device=self.device)))
             else:
                 width, dt = a.cache_row()
-                caches.append(torch.zeros(num_blocks, 16, width, dtype=dt, device=self.device))
+                nb = num_blocks if compressed_blocks is None else compressed_blocks
+                caches.append(torch.zeros(nb, 16, width, dtype=dt, device=self.device))
         return caches
+
+    def kv_bytes_per_token(self) -> int:
+        """Cache bytes this rank holds per token of context, over all layers."""
+        tot = 0.0
+        for ly in self.layers:
+            a = ly["attn"]
+            if ly["full"]:
+                tot += 2 * a.heads * HEAD_DIM * 2
+            else:
+                width, dt = a.cache_row()
+                share = 1.0 / self.world if self.attn_parallel == "context" else 1.0
+                tot += width * torch.empty((), dtype=dt).element_size() * share
+        return int(tot)
 
     def _all_reduce(self, x):
         if self.world > 1:
@@ -178,10 +207,17 @@ class StarKVModel:
             dist.all_reduce(x, group=self.group)
         return x
 
-    def decode_step(self, tokens, positions, caches, block_table, seq_lens, max_seq_len, slot_mapping, ws=None):
+    def decode_step(self, tokens, positions, caches, block_table, seq_lens, max_seq_len, slot_mapping, ws=None,
+                    local=None):
         """One decode step of n sequences: token ids [n] at `positions` (written at
         `slot_mapping`, sequences `seq_lens` long including them); returns the
-        logits [n, vocab] (f32), the same on every rank."""
+        logits [n, vocab] (f32), the same on every rank. With attn_parallel
+        "context", `local` = (block_table, seq_lens, max_seq_len, slot_mapping) of
+        this rank's pages (starkv_b200.context_parallel.local_len / local_index) for
+        the compressed layers; the other arguments serve the full-rank layers."""
+        if self.attn_parallel == "context" and local is None:
+            raise ValueError("attn_parallel='context' needs the local page metadata (`local`)")
+        cmeta = local if local is not None else (block_table, seq_lens, max_seq_len, slot_mapping)
         eps = self.cfg.rms_eps
         x = self.embed[tokens]
         for ly, cache in zip(self.layers, caches):
@@ -190,7 +226,7 @@ class StarKVModel:
                 a = ly["attn"].forward(h, positions, cache[0], cache[1], block_table, seq_lens, max_seq_len,
                                        slot_mapping)
             else:
-                a = ly["attn"].forward(h, positions, cache, block_table, seq_lens, max_seq_len, slot_mapping, ws=ws)
+                a = ly["attn"].forward(h, positions, cache, *cmeta, ws=ws)
             x = x + a
             h = rms_norm(x, ly["norms"][1], eps)
             g, u = F.linear(h, ly["gate_up"]).chunk(2, dim=-1)

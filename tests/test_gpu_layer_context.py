@@ -1,0 +1,88 @@
+"""GPU parity of the page-split (context-parallel) attention layer
+(starkv_b200.layer.StarKVContextLayer), its ranks emulated in one process: each rank
+holds page p % world of every sequence as its own local sequence, writes the new
+token where it owns the page, decodes all heads over its pages with its permuted
+rotary table, and the partials are combined (context_parallel.combine_local, the
+same native combine the all-gather path uses) and go through o_proj.
+
+Reference: the fp64 CPU oracle over the whole layer's cache (the same codes at
+global positions), and the whole layer's own GPU step. Tolerance (the target's):
+2e-2 abs + 1e-2 rel.
+"""
+import numpy as np
+import pytest
+import torch
+
+from test_gpu_layer import HEADS, HIDDEN, LENS, cuda, reference, setup
+
+pytestmark = pytest.mark.gpu
+
+
+def local_setup(w, cs, quant, rank, world, whole_cache, bt, seed=3):
+    """One rank's layer, local cache (rows of positions 0 .. L-2 that it owns, copied
+    from the whole layer's cache), local block table, seq_lens and the new token's slot."""
+    from starkv_b200 import context_parallel as cp
+    from starkv_b200.layer import StarKVContextLayer
+    dev = whole_cache.device
+    ly = StarKVContextLayer(w, cs, quant=quant, rank=rank, world=world)
+    llen = [int(cp.local_len(L, rank, world)) for L in LENS]
+    lpages = [-(-x // 16) for x in llen]
+    tot = max(sum(lpages), 1)
+    perm = torch.randperm(tot, generator=torch.Generator().manual_seed(seed + 10 * rank)) + 1
+    lbt = torch.zeros(len(LENS), max(max(lpages), 1), dtype=torch.int32)
+    k = 0
+    for b, p in enumerate(lpages):
+        lbt[b, :p] = perm[k:k + p]
+        k += p
+    lbt = lbt.to(dev)
+    cache = torch.zeros(tot + 1, 16, whole_cache.shape[-1], dtype=whole_cache.dtype, device=dev)
+    for b, L in enumerate(LENS):
+        pos = torch.arange(L - 1, device=dev)
+        mine = pos[cp.page_owner(pos, world) == rank]
+        if mine.numel():
+            li = cp.local_index(mine, world)
+            cache[lbt[b, li // 16].long(), li % 16] = whole_cache[bt[b, mine // 16].long(), mine % 16]
+    newpos = torch.tensor([L - 1 for L in LENS], device=dev)
+    li = cp.local_index(newpos, world)
+    slots = lbt[torch.arange(len(LENS), device=dev), (li // 16).clamp(max=lbt.shape[1] - 1)].long() * 16 + li % 16
+    slots = torch.where(cp.page_owner(newpos, world) == rank, slots, torch.full_like(slots, -1))
+    seq_lens = torch.tensor(llen, dtype=torch.int32, device=dev)
+    return ly, cache, lbt, seq_lens, max(max(llen), 1), slots
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("quant", [False, True])
+def test_page_split_layer_equals_whole_layer(quant, world):
+    from starkv_b200 import context_parallel as cp
+    from starkv_b200 import layer as Ly
+    from starkv_b200.workload import rope_cos_sin, sample_ranks
+    dev = cuda()
+    layers, caches, bt, seq_lens, new, positions, slots = setup(quant)
+    whole, wcache = layers[0], caches[0]
+    ranks, rv = sample_ranks(HEADS, 3)
+    w = Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=3, device=dev)   # the same weights as setup()'s
+    cs = rope_cos_sin(2048, dev)
+    parts, ranks_state = [], []
+    for r in range(world):
+        ly, cache, lbt, lsl, lmax, lslots = local_setup(w, cs, quant, r, world, wcache, bt)
+        parts.append(ly.forward_partial(new, positions, cache, lbt, lsl, lmax, lslots))
+        ranks_state.append((ly, cache, lbt, lslots))
+    attn = cp.combine_local(parts, dtype=torch.bfloat16)
+    got = torch.nn.functional.linear(attn.reshape(len(LENS), -1), ranks_state[0][0].wo)
+    # the new token's codes went to its owner's local slot only
+    kc, vc = whole.codes(new)
+    for b, L in enumerate(LENS):
+        owner = int(cp.page_owner(L - 1, world))
+        for r, (ly, cache, lbt, lslots) in enumerate(ranks_state):
+            assert (int(lslots[b]) >= 0) == (r == owner)
+        ly, cache, lbt, lslots = ranks_state[owner]
+        row = cache.view(-1, cache.shape[-1])[lslots[b]]
+        if not quant:
+            assert torch.equal(row, torch.cat([kc[b], vc[b]]))
+    ref_out = whole.forward(new, positions, wcache, bt, seq_lens, max(LENS), slots)
+    ref = reference(whole, wcache, bt, new, positions)
+    g = got.double().cpu().numpy()
+    err = np.abs(g - ref)
+    assert np.all(err <= 2e-2 + 1e-2 * np.abs(ref)), f"vs oracle: max abs err {err.max():.3e}"
+    w_err = np.abs(g - ref_out.double().cpu().numpy())
+    assert np.all(w_err <= 2e-2 + 1e-2 * np.abs(ref)), f"vs whole layer: max abs err {w_err.max():.3e}"

@@ -1,6 +1,8 @@
 """Two-GPU check of the whole model's tensor parallelism (starkv_b200.model): two
 NCCL ranks decode the small model sharded (heads LPT / even, MLP columns, o_proj and
-down_proj all-reduced) and get the unsharded model's logits. Needs two GPUs (run as
+down_proj all-reduced) and get the unsharded model's logits. With the page split
+(attn_parallel="context") the compressed layers instead keep page p of every
+sequence on rank p % 2 and combine the ranks' partials. Needs two GPUs (run as
 child processes; skipped on one GPU)."""
 import os
 import socket
@@ -20,20 +22,31 @@ def _free_port():
 
 
 def _decode(model, dev):
+    from starkv_b200 import context_parallel as cp
     g = torch.Generator(device=dev).manual_seed(1)
     tokens = torch.randint(0, model.cfg.vocab, (BATCH, STEPS), generator=g, device=dev)
     pages = -(-STEPS // 16)
-    caches = model.allocate_caches(BATCH * pages + 1)
+    rank, world = model.rank, model.world
+    lpages = max(-(-int(cp.local_len(STEPS, rank, world)) // 16), 1)
+    caches = model.allocate_caches(BATCH * pages + 1, BATCH * lpages + 1)
     bt = torch.arange(BATCH * pages, device=dev, dtype=torch.int32).view(BATCH, pages) + 1
+    lbt = torch.arange(BATCH * lpages, device=dev, dtype=torch.int32).view(BATCH, lpages) + 1
     for t in range(STEPS):
         pos = torch.full((BATCH,), t, device=dev)
         slots = bt[:, t // 16].long() * 16 + t % 16
         seq_lens = torch.full((BATCH,), t + 1, dtype=torch.int32, device=dev)
-        logits = model.decode_step(tokens[:, t], pos, caches, bt, seq_lens, STEPS, slots)
+        local = None
+        if model.attn_parallel == "context":
+            li = int(cp.local_index(t, world))
+            mine = int(cp.page_owner(t, world)) == rank
+            lslots = lbt[:, li // 16].long() * 16 + li % 16 if mine else torch.full_like(slots, -1)
+            llen = int(cp.local_len(t + 1, rank, world))
+            local = (lbt, torch.full((BATCH,), llen, dtype=torch.int32, device=dev), STEPS, lslots)
+        logits = model.decode_step(tokens[:, t], pos, caches, bt, seq_lens, STEPS, slots, local=local)
     return logits
 
 
-def _worker(rank, port, quant, q):
+def _worker(rank, port, quant, split, q):
     import sys
     from datetime import timedelta
     import torch.distributed as dist
@@ -46,7 +59,8 @@ def _worker(rank, port, quant, q):
     dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev, timeout=timedelta(seconds=60))
     try:
         cfg = dict(hidden=512, heads=4, ffn=1024, vocab=512, layers=3, full_layers=(0,), max_pos=256, seed=5)
-        tp = _decode(StarKVModel(ModelConfig(**cfg), dev, quant=quant, rank=rank, world=2), dev)
+        tp = _decode(StarKVModel(ModelConfig(**cfg), dev, quant=quant, rank=rank, world=2, attn_parallel=split),
+                     dev)
         if rank == 0:
             whole = _decode(StarKVModel(ModelConfig(**cfg), dev, quant=quant), dev)
             rel = float((tp - whole).norm() / whole.norm())
@@ -56,15 +70,16 @@ def _worker(rank, port, quant, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("split", ["heads", "context"])
 @pytest.mark.parametrize("quant", [False, True])
-def test_model_tp2_matches_single_gpu(quant):
+def test_model_tp2_matches_single_gpu(quant, split):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, quant, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, quant, split, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -90,3 +90,38 @@ def test_model_config_rank_sampler():
         rvs.append(rv)
     assert 850 < sum(Ws) / 32 < 1150 and 1100 < sum(rvs) / 32 < 1450    # comp-ratio 0.75 sizes
     assert cfg.layer_ranks(5) == ModelConfig().layer_ranks(5)           # seeded: every rank agrees
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_page_round_robin_placement(world):
+    """Every global position has one owner and a distinct local index there, the local
+    tokens of a rank are a contiguous prefix of length local_len, global_position
+    inverts local_index, and the rank's rotary table row i is the global row of its
+    local token i."""
+    from starkv_b200 import context_parallel as cp
+    for L in [0, 1, 15, 16, 17, 47, 48, 200, 1029]:
+        pos = torch.arange(L)
+        owner = cp.page_owner(pos, world)
+        for r in range(world):
+            mine = pos[owner == r]
+            li = cp.local_index(mine, world)
+            assert torch.equal(li, torch.arange(mine.numel()))                  # contiguous local prefix
+            assert int(cp.local_len(L, r, world)) == mine.numel()
+            assert torch.equal(cp.global_position(li, r, world), mine)
+        lens = torch.tensor([L, L + 1])
+        assert torch.equal(cp.local_len(lens, 0, world),
+                           torch.tensor([int(cp.local_len(L, 0, world)), int(cp.local_len(L + 1, 0, world))]))
+    cs = torch.randn(100, 128)
+    for r in range(world):
+        t = cp.local_rotary_table(cs, r, world)
+        i = torch.arange(t.shape[0])
+        g = cp.global_position(i, r, world)
+        ok = g < 100
+        assert torch.equal(t[ok], cs[g[ok]])
+        assert t.shape[0] * world >= 100
+
+
+def test_model_rejects_unknown_attention_split():
+    from starkv_b200.model import ModelConfig, StarKVModel
+    with pytest.raises(ValueError):
+        StarKVModel(ModelConfig(layers=1), "cpu", attn_parallel="rows")
