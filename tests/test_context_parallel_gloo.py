@@ -111,3 +111,62 @@ def test_two_rank_context_split_matches_unsplit_decode():
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         assert result["scale"] > 0
         assert result["err"] <= 1e-10 * max(1.0, result["scale"]), result["err"]
+
+
+def _page_rank_main(rank, port, result):
+    """Page round-robin placement (the whole model's split for growing sequences):
+    the rank's pages of a sequence, as one local sequence, with the rank's permuted
+    rotary table (context_parallel.local_rotary_table), give partials that combine
+    to the unsplit decode."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60))
+    try:
+        import starkv_oracle as O
+        from starkv_b200 import context_parallel as cp
+        ranks, offsets, seqs, k_up, v_up, cs, scale = _inputs()
+        cs_local = cp.local_rotary_table(torch.tensor(cs), rank, WORLD).numpy()
+        outs, ms, ls = [], [], []
+        for (q, k, v), L in zip(seqs, LENS):
+            pos = np.arange(L)
+            mine = pos[cp.page_owner(pos, WORLD) == rank]
+            assert np.array_equal(cp.local_index(mine, WORLD), np.arange(mine.size))
+            n_loc = int(cp.local_len(L, rank, WORLD))
+            assert n_loc == mine.size
+            o, m, l = _partial(q, k[mine], v[mine], k_up, ranks, offsets, v_up, cs_local, scale, 0, n_loc)
+            outs.append(o); ms.append(m); ls.append(l)
+        parts = cp.gather_partials(torch.tensor(np.stack(outs)), torch.tensor(np.stack(ms)),
+                                   torch.tensor(np.stack(ls))).numpy()
+        if rank == 0:
+            n, H = len(LENS), ms[0].shape[0]
+            P = parts.reshape(WORLD, -1)
+            o = P[:, :n * H * 128].reshape(WORLD, n, H, 128)
+            m = P[:, n * H * 128:n * H * 129].reshape(WORLD, n, H)
+            l = P[:, n * H * 129:].reshape(WORLD, n, H)
+            M = m.max(0)
+            s = np.exp(m - M)
+            got = (s[..., None] * o).sum(0) / (s * l).sum(0)[..., None]
+            ref = np.stack([O.attend_one(q, k, v, k_up, ranks, offsets, 1, v_up, cs, scale) for q, k, v in seqs])
+            result["err"] = float(np.abs(got - ref).max())
+            result["scale"] = float(np.abs(ref).max())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_page_split_matches_unsplit_decode():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_page_rank_main, args=(r, port, result)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=180)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert result["scale"] > 0
+        assert result["err"] <= 1e-10 * max(1.0, result["scale"]), result["err"]
