@@ -86,3 +86,77 @@ def test_page_split_layer_equals_whole_layer(quant, world):
     assert np.all(err <= 2e-2 + 1e-2 * np.abs(ref)), f"vs oracle: max abs err {err.max():.3e}"
     w_err = np.abs(g - ref_out.double().cpu().numpy())
     assert np.all(w_err <= 2e-2 + 1e-2 * np.abs(ref)), f"vs whole layer: max abs err {w_err.max():.3e}"
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_page_split_prefill_then_decode(quant):
+    """Prompts prefilled through each rank's StarKVContextLayer (the inherited dense
+    prefill, given the rank's local slots and -1 elsewhere), then one decode step:
+    every rank's cache rows equal the whole layer's rows at the positions it owns,
+    the prefill output equals the whole layer's, and the decode matches it."""
+    from starkv_b200 import context_parallel as cp
+    from starkv_b200 import layer as Ly
+    from starkv_b200.workload import rope_cos_sin, sample_ranks
+    dev = cuda()
+    world, P = 2, [37, 70, 16]
+    ranks, rv = sample_ranks(HEADS, 5)
+    w = Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=5, device=dev)
+    cs = rope_cos_sin(1024, dev)
+    g = torch.Generator(device=dev).manual_seed(6)
+    prompt = torch.randn(sum(P), HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    new = torch.randn(len(P), HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    ppos = torch.cat([torch.arange(L, device=dev) for L in P])
+    seq_of = torch.cat([torch.full((L,), b, device=dev) for b, L in enumerate(P)])
+    npos = torch.tensor(P, device=dev)                        # the decode token of each sequence
+
+    whole = Ly.StarKVAttentionLayer(w, cs, quant=quant)
+    pages = [-(-(L + 1) // 16) for L in P]
+    bt = torch.zeros(len(P), max(pages), dtype=torch.int32)
+    k = 1
+    for b, p in enumerate(pages):
+        bt[b, :p] = torch.arange(k, k + p)
+        k += p
+    bt = bt.to(dev)
+    width, dt = whole.cache_row()
+    wcache = torch.zeros(k, 16, width, dtype=dt, device=dev)
+    pre_whole = whole.prefill(prompt, ppos, P, wcache, bt[seq_of, ppos // 16].long() * 16 + ppos % 16)
+    dec_whole = whole.forward(new, npos, wcache, bt, torch.tensor([L + 1 for L in P], dtype=torch.int32, device=dev),
+                              max(P) + 1, bt[torch.arange(len(P), device=dev), npos // 16].long() * 16 + npos % 16)
+
+    parts = []
+    for r in range(world):
+        ly = Ly.StarKVContextLayer(w, cs, quant=quant, rank=r, world=world)
+        llen = [int(cp.local_len(L + 1, r, world)) for L in P]
+        lpages = [max(-(-x // 16), 1) for x in llen]
+        lbt = torch.zeros(len(P), max(lpages), dtype=torch.int32)
+        k = 1
+        for b, p in enumerate(lpages):
+            lbt[b, :p] = torch.arange(k, k + p)
+            k += p
+        lbt = lbt.to(dev)
+        cache = torch.zeros(k, 16, width, dtype=dt, device=dev)
+
+        def local_slots(seq, pos):
+            li = cp.local_index(pos, world)
+            s = lbt[seq, (li // 16).clamp(max=lbt.shape[1] - 1)].long() * 16 + li % 16
+            return torch.where(cp.page_owner(pos, world) == r, s, torch.full_like(s, -1))
+
+        pre = ly.prefill(prompt, ppos, P, cache, local_slots(seq_of, ppos))
+        torch.testing.assert_close(pre, pre_whole, rtol=1e-2, atol=1e-3)   # the same math on the same inputs
+        seqs = torch.arange(len(P), device=dev)
+        parts.append(ly.forward_partial(new, npos, cache, lbt, torch.tensor(llen, dtype=torch.int32, device=dev),
+                                        max(max(llen), 1), local_slots(seqs, npos)))
+        # the rank's rows (prompt and decode token) are the whole layer's rows at its positions
+        for b, L in enumerate(P):
+            pos = torch.arange(L + 1, device=dev)
+            mine = pos[cp.page_owner(pos, world) == r]
+            li = cp.local_index(mine, world)
+            got = cache[lbt[b, li // 16].long(), li % 16]
+            ref = wcache[bt[b, mine // 16].long(), mine % 16]
+            assert torch.equal(got, ref), (r, b)
+        last_ly = ly
+    attn = cp.combine_local(parts, dtype=torch.bfloat16)
+    got = torch.nn.functional.linear(attn.reshape(len(P), -1), last_ly.wo).double()
+    ref = dec_whole.double()
+    err = (got - ref).abs()
+    assert bool((err <= 2e-2 + 1e-2 * ref.abs()).all()), f"max abs err {float(err.max()):.3e}"
