@@ -131,3 +131,68 @@ def local_rotary_table(cos_sin_cache: torch.Tensor, rank: int, world: int, block
     rows = -(-P // (block_size * world)) * block_size
     i = torch.arange(rows, device=cos_sin_cache.device)
     return cos_sin_cache[global_position(i, rank, world, block_size).clamp(max=P - 1)].contiguous()
+
+
+class PageSplitTables:
+    """One rank's block tables under the page split, for sequences that grow.
+
+    A serving engine keeps one of these per rank. `extend` appends tokens to
+    sequences and returns the local cache slots to write them at. A slot is -1 where
+    another rank owns the token's page; the cache-write kernels send such a slot to
+    the reserved null block. A rank takes a local block only when one of its pages
+    starts. `decode_metadata` returns the local block table, sequence lengths and
+    their bound for a decode call over the rank's pages. `release` frees a finished
+    sequence's blocks for reuse. Block 0 is never handed out: it stays the null
+    block."""
+
+    def __init__(self, rank: int, world: int, num_blocks: int, block_size: int = 16):
+        if not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside a world of {world}")
+        self.rank, self.world, self.block_size = rank, world, block_size
+        self.free = list(range(num_blocks - 1, 0, -1))     # pop() hands out low ids first
+        self.blocks: dict = {}                              # sequence id -> local block ids
+        self.lens: dict = {}                                # sequence id -> global length
+
+    def extend(self, seq_id, count: int = 1) -> list[int]:
+        """Append `count` tokens to `seq_id` (created on first use); returns the local
+        slot of each new token, -1 where another rank stores it."""
+        L = self.lens.get(seq_id, 0)
+        bs = self.block_size
+        held = len(self.blocks.get(seq_id, []))
+        need = -(-int(local_len(L + count, self.rank, self.world, bs)) // bs) - held
+        if need > len(self.free):   # refuse before changing anything
+            raise RuntimeError(f"rank {self.rank}: sequence {seq_id!r} needs {need} more cache blocks, "
+                               f"{len(self.free)} free")
+        blocks = self.blocks.setdefault(seq_id, [])
+        blocks.extend(self.free.pop() for _ in range(need))
+        out = []
+        for pos in range(L, L + count):
+            if page_owner(pos, self.world, bs) != self.rank:
+                out.append(-1)
+            else:
+                li = local_index(pos, self.world, bs)
+                out.append(blocks[li // bs] * bs + li % bs)
+        self.lens[seq_id] = L + count
+        return out
+
+    def local_len(self, seq_id) -> int:
+        return int(local_len(self.lens.get(seq_id, 0), self.rank, self.world, self.block_size))
+
+    def decode_metadata(self, seq_ids, device=None, max_blocks: int | None = None):
+        """(block_table int32 [n, max_blocks], seq_lens int32 [n], max_seq_len) of the
+        rank's local sequences, for paged_starkv_decode / paged_quant_decode."""
+        lens = [self.local_len(s) for s in seq_ids]
+        width = max_blocks or max([len(self.blocks.get(s, [])) for s in seq_ids] + [1])
+        bt = torch.zeros(len(seq_ids), width, dtype=torch.int32)
+        for i, s in enumerate(seq_ids):
+            b = self.blocks.get(s, [])
+            if len(b) > width:
+                raise ValueError(f"sequence {s!r} holds {len(b)} blocks here, more than max_blocks={width}")
+            bt[i, :len(b)] = torch.tensor(b, dtype=torch.int32)
+        return (bt.to(device) if device is not None else bt,
+                torch.tensor(lens, dtype=torch.int32, device=device), max(lens + [1]))
+
+    def release(self, seq_id) -> None:
+        """Forget a finished sequence and free its blocks."""
+        self.free.extend(reversed(self.blocks.pop(seq_id, [])))
+        self.lens.pop(seq_id, None)

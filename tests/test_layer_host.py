@@ -125,3 +125,67 @@ def test_model_rejects_unknown_attention_split():
     from starkv_b200.model import ModelConfig, StarKVModel
     with pytest.raises(ValueError):
         StarKVModel(ModelConfig(layers=1), "cpu", attn_parallel="rows")
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_page_split_tables_place_growing_sequences(world):
+    """Sequences grow by prompts and single decode tokens while others finish. Every
+    token is written on exactly one rank, at a slot that no other live token holds.
+    Reading a rank's cache through its decode block table gives the rank's tokens in
+    local order, with global positions global_position(i). Freed blocks are reused,
+    and a rank with too few blocks refuses without changing its state."""
+    import random
+    import numpy as np
+    from starkv_b200 import context_parallel as cp
+    rng = random.Random(world)
+    nb = 64
+    tabs = [cp.PageSplitTables(r, world, nb) for r in range(world)]
+    caches = [np.full((nb, 16), -1, dtype=np.int64) for _ in range(world)]   # global position stored per slot
+    live, next_id = {}, 0
+    for step in range(300):
+        if len(live) < 4 and rng.random() < 0.3:
+            sid, n = next_id, rng.randint(1, 60)
+            next_id += 1
+            live[sid] = 0
+        elif live and rng.random() < 0.05:
+            sid = rng.choice(list(live))
+            for t in tabs:
+                t.release(sid)
+            del live[sid]
+            continue
+        elif live:
+            sid, n = rng.choice(list(live)), 1
+        else:
+            continue
+        try:
+            slots = [t.extend(sid, n) for t in tabs]
+        except RuntimeError:
+            continue                      # a rank is full; the tables are unchanged
+        L0 = live[sid]
+        for i in range(n):
+            owners = [r for r in range(world) if slots[r][i] >= 0]
+            assert owners == [int(cp.page_owner(L0 + i, world))]
+            r = owners[0]
+            caches[r].reshape(-1)[slots[r][i]] = L0 + i
+        live[sid] = L0 + n
+        # every live sequence reads back in local order on every rank
+        for r, t in enumerate(tabs):
+            ids = list(live)
+            bt, lens, mx = t.decode_metadata(ids)
+            for k, s in enumerate(ids):
+                ln = int(lens[k])
+                assert ln == int(cp.local_len(live[s], r, world))
+                idx = np.arange(ln)
+                got = caches[r][bt[k, idx // 16].numpy(), idx % 16]
+                assert np.array_equal(got, cp.global_position(idx, r, world)), (step, r, s)
+            assert mx >= max([int(x) for x in lens] + [1])
+            held = [b for s in ids for b in t.blocks.get(s, [])]
+            assert len(held) == len(set(held)) and 0 not in held      # no block twice, null block kept
+            assert len(held) + len(t.free) == nb - 1                  # freed blocks go back to the pool
+    # a refused extension leaves the tables as they were
+    t = cp.PageSplitTables(0, world, 3)
+    t.extend("a", 16)
+    before = (dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free))
+    with pytest.raises(RuntimeError):
+        t.extend("a", 16 * world * 4)
+    assert before == (dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free))
