@@ -160,3 +160,53 @@ def test_page_split_prefill_then_decode(quant):
     ref = dec_whole.double()
     err = (got - ref).abs()
     assert bool((err <= 2e-2 + 1e-2 * ref.abs()).all()), f"max abs err {float(err.max()):.3e}"
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_page_split_tables_drive_prefill_and_growing_decode(quant):
+    """Two emulated ranks, each with a context_parallel.PageSplitTables, prefill two
+    prompts and then decode 24 steps. The steps cross page boundaries, so ownership of
+    the new token alternates between the ranks. Every step's combined output matches
+    the whole layer's step."""
+    from starkv_b200 import context_parallel as cp
+    from starkv_b200 import layer as Ly
+    from starkv_b200.workload import rope_cos_sin, sample_ranks
+    dev = cuda()
+    world, P, steps = 2, [20, 45], 24
+    ranks, rv = sample_ranks(HEADS, 7)
+    w = Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=7, device=dev)
+    cs = rope_cos_sin(1024, dev)
+    g = torch.Generator(device=dev).manual_seed(8)
+    prompt = torch.randn(sum(P), HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    ppos = torch.cat([torch.arange(L, device=dev) for L in P])
+    whole = Ly.StarKVAttentionLayer(w, cs, quant=quant)
+    width, dt = whole.cache_row()
+    wtab = cp.PageSplitTables(0, 1, 64)                 # world 1: the whole layer's own tables
+    wcache = torch.zeros(64, 16, width, dtype=dt, device=dev)
+    lys = [Ly.StarKVContextLayer(w, cs, quant=quant, rank=r, world=world) for r in range(world)]
+    tabs = [cp.PageSplitTables(r, world, 64) for r in range(world)]
+    caches = [torch.zeros(64, 16, width, dtype=dt, device=dev) for _ in range(world)]
+
+    def slots_of(tab, counts):
+        return torch.tensor([s for b, c in enumerate(counts) for s in tab.extend(b, c)], device=dev)
+
+    whole.prefill(prompt, ppos, P, wcache, slots_of(wtab, P))
+    for ly, tab, cache in zip(lys, tabs, caches):
+        ly.prefill(prompt, ppos, P, cache, slots_of(tab, P))
+    lens = list(P)
+    for step in range(steps):
+        new = torch.randn(len(P), HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        pos = torch.tensor(lens, device=dev)
+        ws = slots_of(wtab, [1] * len(P))
+        bt, sl, mx = wtab.decode_metadata(range(len(P)), dev)
+        ref = whole.forward(new, pos, wcache, bt, sl, mx, ws).double()
+        parts = []
+        for ly, tab, cache in zip(lys, tabs, caches):
+            ls = slots_of(tab, [1] * len(P))
+            lbt, lsl, lmx = tab.decode_metadata(range(len(P)), dev)
+            parts.append(ly.forward_partial(new, pos, cache, lbt, lsl, lmx, ls))
+        attn = cp.combine_local(parts, dtype=torch.bfloat16)
+        got = torch.nn.functional.linear(attn.reshape(len(P), -1), lys[0].wo).double()
+        err = (got - ref).abs()
+        assert bool((err <= 2e-2 + 1e-2 * ref.abs()).all()), f"step {step}: max abs err {float(err.max()):.3e}"
+        lens = [L + 1 for L in lens]
