@@ -35,7 +35,7 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-CLOCKS_DIR = os.environ.get("STARKV_CLOCKS_DIR", os.path.join(ROOT, "gpurun_out"))
+CLOCKS_DIR = os.environ.get("STARKV_CLOCKS_DIR", os.path.join(ROOT, "clocks"))
 sys.path.insert(0, os.path.join(ROOT, "star-kv-serve_b200"))
 
 METRIC = "low-rank paged decode attn µs/layer & HBM GB/s; decode tok/s at 1/2/4/8 B200"
@@ -268,7 +268,9 @@ def measure(layer, device, steps, warmup, dist_on, cp=None):
     e2e_ms = timed(e2e_step, steps)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hbt, hsl))
     d2h = hout.numel() * hout.element_size()
-    return ms, per_kernel, clocks, e2e_ms, h2d, d2h
+    last = step()
+    torch.cuda.synchronize()
+    return ms, per_kernel, clocks, e2e_ms, h2d, d2h, last
 
 
 def layer_case(args, device, world, rank, dist_on):
@@ -484,6 +486,65 @@ def roofline_for(layer, per_kernel, hbm_peak, cp=None):
             "kernel_ms": {nm: round(v, 4) for nm, v in zip(names, per_kernel)}}
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def triton_bar(layer, device, steps, ours_decode_ms, ours_out=None):
+    """The reference's own GPU decode on the same inputs: paged_starkv_decode
+    (paged_decode.py:150-226) or paged_quant_decode (paged_quant.py:357-411), imported
+    unmodified from the installed reference (baseline/_ref) and JIT-compiled by this
+    box's Triton. Timed with CUDA events after a warm-up that includes compilation;
+    decode only (no cache write), beside our decode-only time (sum of our 4 kernels).
+    The output is compared with ours as a sanity check (max abs difference)."""
+    import torch
+    if not os.path.isdir(os.path.join(REF_DIR, "starkv_serve")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from starkv_serve.kernels import paged_decode as rpd
+        from starkv_serve.kernels import paged_quant as rpq
+    except Exception as e:   # noqa: BLE001 - reported, not fatal
+        return {"unavailable": f"import failed: {type(e).__name__}: {e}"[:300]}
+    L = layer
+    if L.quant:
+        row = rpq.QuantRow(L.k_width, len(L.ranks), L.v_rank)
+        _, hol, tiles = rpq.k_tables(L.ranks, device)
+
+        def fn():
+            return rpq.paged_quant_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, row,
+                                          L.k_up, hol, tiles, L.v_up_by_q, L.cos_sin_cache, L.scale)
+    else:
+        def fn():
+            return rpd.paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up,
+                                           L.k_ranks, L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache,
+                                           L.scale)
+    try:
+        t0 = time.perf_counter()
+        out = fn()
+        torch.cuda.synchronize()
+        compile_s = time.perf_counter() - t0
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    except Exception as e:   # noqa: BLE001 - a compile or launch failure is the result
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    res = {"impl": "reference Triton (baseline/_ref, unmodified), this box's Triton JIT",
+           "ms_per_decode": round(ms, 4), "ours_decode_ms": round(ours_decode_ms, 4),
+           "speedup": round(ms / ours_decode_ms, 3) if ours_decode_ms > 0 else None,
+           "first_call_s": round(compile_s, 2), "steps": steps}
+    if ours_out is not None:
+        res["max_abs_diff_vs_ours"] = float((out.float() - ours_out.float()).abs().max())
+    return res
+
+
 def cpu_sample_time(quant: bool, seconds: float = 12.0):
     """Reference algorithm (oracle port, numpy, all host cores) on whole sequences of
     the same workload; returns (sequences per second, sample description)."""
@@ -549,10 +610,14 @@ def ours(args):
                                    mixed=args.case == "c4")
         cp = (rank, world) if dist_on and args.parallel == "context" else None
         # sequence split (seqs): every rank decodes its own whole batch
-        ms, per_kernel, clocks, e2e_ms, h2d, d2h = measure(layer, device, args.steps, args.warmup, dist_on, cp)
+        ms, per_kernel, clocks, e2e_ms, h2d, d2h, last = measure(layer, device, args.steps, args.warmup, dist_on,
+                                                                 cp)
         res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
                           d2h=d2h, alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
                           roof=roofline_for(layer, per_kernel, hbm_peak, cp))
+        if world == 1 and args.case in ("both", "c2", "c3") and not args.no_bar:
+            res[quant]["bar"] = triton_bar(layer, device, args.steps, sum(per_kernel), last)
+        del last
         del layer
         torch.cuda.empty_cache()
     if rank == 0 and args.case == "c4":
@@ -577,7 +642,8 @@ def ours(args):
         r = res[cases[0]]
         print(json.dumps({"case": args.case, "batch": r["layer"].n, "context": r["layer"].seq_lens_host[0],
                           "ms_per_step": round(r["ms"], 4), "kernel_ms": r["roof"]["kernel_ms"],
-                          "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1)}), flush=True)
+                          "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
+                          "roofline_frac": r["roof"]["frac"], "gpu_bar": r.get("bar")}), flush=True)
     elif rank == 0:
         b = res[False]
         n = b["layer"].n
@@ -606,6 +672,7 @@ def ours(args):
             "e2e": {"value": round(reps * n / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": b["h2d"], "d2h_bytes_per_step": b["d2h"],
                     "ms_per_step": round(b["e2e_ms"], 4)},
+            "gpu_bar": {"bf16": b.get("bar"), "q32": q.get("bar")} if world == 1 and not args.no_bar else None,
             "gpu_launches": (5 if world == 1 or args.parallel != "context" or rank == world - 1 else 4) * args.steps,
             "clocks": b["clocks"],
             "q32": {"workload": "config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
@@ -660,6 +727,7 @@ def main():
                          "the GPUs by each sequence's tiles (context) or by heads")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling small cases)")
     ap.add_argument("--context", type=int, default=None, help="override the context (profiling small cases)")
+    ap.add_argument("--no-bar", action="store_true", help="skip timing the reference's Triton kernels")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define STARKV_ABI_VERSION 1
+#define STARKV_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define STARKV_API __attribute__((visibility("default")))
@@ -119,10 +119,21 @@ STARKV_API int starkv_paged_decode_bf16(const StarKVDecodeArgs* args, void* work
  * The first call on a device looks the array's address up (with that device
  * current) and should come before any stream capture. All calls share the
  * array: calls whose kernels overlap on the GPU race; keep them ordered on one
- * stream. Its device status word is cleared at the start of each call.
+ * stream. Its device status word is cleared at the start of each call and read
+ * with starkv_noalloc_read_status below. A failed first address lookup is
+ * retried by the next call.
  */
 #define STARKV_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 STARKV_API int starkv_paged_decode_bf16_noalloc(const StarKVDecodeArgs* args, void* stream);
+
+/*
+ * No counterpart in the reference. Device status word of the built-in scratch
+ * on the current device: what the last starkv_paged_decode_bf16_noalloc call's
+ * kernels recorded (STARKV_EBOUNDS: a block id outside the cache was skipped;
+ * STARKV_ETIMEOUT: a pipeline wait expired), 0 if nothing. Synchronises the
+ * stream (tests, debugging); clears the word when reset != 0.
+ */
+STARKV_API int starkv_noalloc_read_status(int32_t* host_status, int32_t reset, void* stream);
 
 /* paged_quant.py:357-411 -- 3.2-bit codes (MHA, head_dim 128). */
 STARKV_API int starkv_paged_decode_q32(const StarKVDecodeArgs* args, void* workspace, size_t workspace_bytes,
@@ -174,11 +185,14 @@ STARKV_API int starkv_cp_combine(const float* parts, int32_t world, int32_t n, i
  * head_of_lane [W] -> ab [n, W, 128] f16 (contiguous), the logit scale folded in:
  *   A[r,i] = (q_i U[r,i] + q_{i+64} U[r,i+64]) * scale
  *   B[r,i] = (q_{i+64} U[r,i] - q_i U[r,i+64]) * scale
+ * q and k_up are bf16, f16 or f32 (else STARKV_EDTYPE); W is a multiple of 16.
+ * A head_of_lane entry outside [0, H) gives a zero row and is recorded as
+ * STARKV_EBOUNDS in *status (optional device int32; null: not recorded).
  */
 STARKV_API int starkv_fold_q(const void* query, const int64_t q_stride[3], int32_t q_dtype,
                   const void* k_up, const int64_t k_up_stride[2], int32_t k_up_dtype,
                   const int32_t* head_of_lane, int32_t n, int32_t num_heads, int32_t k_width,
-                  float scale, void* ab_out, void* stream);
+                  float scale, void* ab_out, int32_t* status, void* stream);
 
 /* paged_quant.py:205-216 (pack_kv): quantize n tokens' codes into their slots. */
 typedef struct StarKVPackArgs {

@@ -328,6 +328,28 @@ def decode_paged_quant(query, kv_cache_u8, block_table, seq_lens, row: QuantRow,
     return np.stack(outs)
 
 
+def fold_q(q: np.ndarray, k_up: np.ndarray, head_of_lane: np.ndarray, scale: float) -> np.ndarray:
+    """Oracle for `fold_q` / `_fold_q` (paged_quant.py:223-255): the query folded
+    into the K up-projection, A|B [n, W, 128] rounded to float16, with
+
+        A[r, i] = (q_i U[r, i] + q_{i+64} U[r, i+64]) * scale
+        B[r, i] = (q_{i+64} U[r, i] - q_i U[r, i+64]) * scale
+
+    q [n, H, 128] and k_up [W, 128] as float32 (bf16 inputs upcast); head_of_lane
+    [W] picks each lane's query head. Products and sums in float32 as the Triton
+    kernel does (it may fuse one multiply-add, so results can differ from a fused
+    implementation by one float16 ulp)."""
+    q = np.asarray(q, np.float32)
+    u = np.asarray(k_up, np.float32)
+    qh = q[:, np.asarray(head_of_lane, np.int64), :]           # [n, W, 128]
+    a0, a1 = qh[..., :64], qh[..., 64:]
+    u0, u1 = u[None, :, :64], u[None, :, 64:]
+    sc = np.float32(scale)
+    A = ((a0 * u0 + a1 * u1) * sc).astype(np.float16)
+    B = ((a1 * u0 - a0 * u1) * sc).astype(np.float16)
+    return np.concatenate([A, B], axis=-1)
+
+
 def rope_cos_sin(max_pos: int, head_dim: int = HEAD_DIM, base: float = 10000.0,
                  linear_factor: float = 1.0) -> np.ndarray:
     """vLLM-style rotary `cos_sin_cache` [max_pos, head_dim] = cat(cos, sin) for

@@ -382,10 +382,16 @@ int starkv_paged_decode_q32_partial(const StarKVDecodeArgs* args, int32_t cp_ran
 
 int starkv_fold_q(const void* query, const int64_t q_stride[3], int32_t q_dtype, const void* k_up,
                   const int64_t k_up_stride[2], int32_t k_up_dtype, const int32_t* head_of_lane, int32_t n,
-                  int32_t num_heads, int32_t k_width, float scale, void* ab_out, void* stream) {
+                  int32_t num_heads, int32_t k_width, float scale, void* ab_out, int32_t* status, void* stream) {
   using namespace starkv;
-  if (!query || !k_up || !head_of_lane || !ab_out || n < 0 || num_heads <= 0 || k_width <= 0) return STARKV_EINVAL;
+  if (!query || !k_up || !head_of_lane || !ab_out || !q_stride || !k_up_stride || n < 0 || num_heads <= 0 ||
+      k_width <= 0 || k_width % 16)
+    return STARKV_EINVAL;
+  if (!is_float_dtype(q_dtype) || !is_float_dtype(k_up_dtype)) return STARKV_EDTYPE;
+  if (reinterpret_cast<uintptr_t>(ab_out) & 15) return STARKV_EALIGN;
   if (n == 0) return STARKV_OK;
+  DeviceInfo dev;
+  if (const int st = device_info(dev)) return st;
   FoldParams fp{};
   fp.q = query; fp.q_s0 = q_stride[0]; fp.q_s1 = q_stride[1]; fp.q_s2 = q_stride[2]; fp.q_dtype = q_dtype;
   fp.k_up = k_up; fp.ku_s0 = k_up_stride[0]; fp.ku_s1 = k_up_stride[1]; fp.k_up_dtype = k_up_dtype;
@@ -393,6 +399,7 @@ int starkv_fold_q(const void* query, const int64_t q_stride[3], int32_t q_dtype,
   fp.n = n; fp.num_heads = num_heads; fp.num_kv_heads = num_heads; fp.group = 1; fp.k_width = k_width;
   fp.head_dim = 128; fp.scale = scale; fp.ab = reinterpret_cast<__half*>(ab_out);
   fp.l_pad = 0; fp.m_count = 0; fp.pv_count = 0;
+  fp.status = status;   // a head_of_lane entry outside [0, num_heads) is recorded here (its row is zero)
   return launch_fold(fp, true, (cudaStream_t)stream);
 }
 
@@ -451,7 +458,7 @@ size_t starkv_abi_sizeof(int32_t which) {
   }
 }
 
-const char* starkv_version(void) { return "starkv_b200 1.0 (abi 1, sm_100a)"; }
+const char* starkv_version(void) { return "starkv_b200 1.1 (abi 2, sm_100a)"; }
 
 const char* starkv_strerror(int status) {
   switch (status) {

@@ -81,11 +81,12 @@ EXPORTS = {
     "starkv_paged_decode_bf16": (C.c_int, [C.POINTER(DecodeArgs), p, C.c_size_t, p]),
     "starkv_paged_decode_q32": (C.c_int, [C.POINTER(DecodeArgs), p, C.c_size_t, p]),
     "starkv_paged_decode_bf16_noalloc": (C.c_int, [C.POINTER(DecodeArgs), p]),
+    "starkv_noalloc_read_status": (C.c_int, [C.POINTER(i32), i32, p]),
     "starkv_paged_decode_bf16_partial": (C.c_int, [C.POINTER(DecodeArgs), i32, i32, p, p, p, C.c_size_t, p]),
     "starkv_paged_decode_q32_partial": (C.c_int, [C.POINTER(DecodeArgs), i32, i32, p, p, p, C.c_size_t, p]),
     "starkv_cp_combine": (C.c_int, [p, i32, i32, i32, p, C.POINTER(i64), i32, p]),
     "starkv_selftest_wait_timeout": (C.c_int, [p, p]),
-    "starkv_fold_q": (C.c_int, [p, C.POINTER(i64), i32, p, C.POINTER(i64), i32, p, i32, i32, i32, f32, p, p]),
+    "starkv_fold_q": (C.c_int, [p, C.POINTER(i64), i32, p, C.POINTER(i64), i32, p, i32, i32, i32, f32, p, p, p]),
     "starkv_pack_kv_q32": (C.c_int, [C.POINTER(PackArgs), p]),
     "starkv_cache_write_bf16": (C.c_int, [C.POINTER(CacheWriteArgs), p]),
     "starkv_read_status": (C.c_int, [p, C.POINTER(i32), i32, p]),

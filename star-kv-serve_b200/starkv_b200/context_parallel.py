@@ -153,13 +153,28 @@ class PageSplitTables:
         self.blocks: dict = {}                              # sequence id -> local block ids
         self.lens: dict = {}                                # sequence id -> global length
 
+    def blocks_needed(self, seq_id, count: int = 1) -> int:
+        """Local blocks this rank would take to append `count` tokens to `seq_id`;
+        changes nothing."""
+        L = self.lens.get(seq_id, 0)
+        held = len(self.blocks.get(seq_id, []))
+        return -(-int(local_len(L + count, self.rank, self.world, self.block_size)) // self.block_size) - held
+
+    def can_extend(self, seq_id, count: int = 1) -> bool:
+        """Whether this rank has the blocks for `extend(seq_id, count)`; changes nothing.
+        The ranks of a group must agree before any of them extends (each rank's need
+        differs), see extend_agreed / extend_on_all_ranks."""
+        return self.blocks_needed(seq_id, count) <= len(self.free)
+
     def extend(self, seq_id, count: int = 1) -> list[int]:
         """Append `count` tokens to `seq_id` (created on first use); returns the local
-        slot of each new token, -1 where another rank stores it."""
+        slot of each new token, -1 where another rank stores it. Refuses with
+        RuntimeError, changing nothing, when this rank is short of blocks; that keeps
+        one rank consistent, not the group (another rank may already have extended),
+        so a serving engine extends through extend_agreed."""
         L = self.lens.get(seq_id, 0)
         bs = self.block_size
-        held = len(self.blocks.get(seq_id, []))
-        need = -(-int(local_len(L + count, self.rank, self.world, bs)) // bs) - held
+        need = self.blocks_needed(seq_id, count)
         if need > len(self.free):   # refuse before changing anything
             raise RuntimeError(f"rank {self.rank}: sequence {seq_id!r} needs {need} more cache blocks, "
                                f"{len(self.free)} free")
@@ -196,3 +211,29 @@ class PageSplitTables:
         """Forget a finished sequence and free its blocks."""
         self.free.extend(reversed(self.blocks.pop(seq_id, [])))
         self.lens.pop(seq_id, None)
+
+
+def extend_on_all_ranks(tables: list[PageSplitTables], seq_id, count: int = 1) -> list[list[int]]:
+    """Extend `seq_id` on every rank's tables held in one process (ranks emulated
+    on one GPU, tests): every rank is checked first, so either all extend or none
+    does (RuntimeError, nothing changed)."""
+    short = [t.rank for t in tables if not t.can_extend(seq_id, count)]
+    if short:
+        raise RuntimeError(f"sequence {seq_id!r}: rank(s) {short} short of cache blocks; no rank extended")
+    return [t.extend(seq_id, count) for t in tables]
+
+
+def extend_agreed(table: PageSplitTables, seq_id, count: int = 1, group=None) -> list[int]:
+    """Extend `seq_id` on this rank only if every rank of the group can: the ranks
+    agree with one MIN all-reduce of can_extend (a tensor on the backend's device)
+    before any of them changes its tables. If any rank is short, every rank raises
+    RuntimeError with its tables unchanged, so the group stays consistent. Every rank
+    must call it for the same (seq_id, count), in the same order."""
+    import torch.distributed as dist
+    ok = torch.tensor([1 if table.can_extend(seq_id, count) else 0], dtype=torch.int32)
+    if dist.get_backend(group) == "nccl":
+        ok = ok.cuda()
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    if int(ok.item()) == 0:
+        raise RuntimeError(f"sequence {seq_id!r}: a rank of the group is short of cache blocks; no rank extended")
+    return table.extend(seq_id, count)

@@ -148,12 +148,14 @@ def pack_kv(k_codes, v_codes, cache, slot_mapping, row: QuantRow, k_ranks, k_off
 # decode
 # ---------------------------------------------------------------------------
 
-def fold_q(q, k_up, head_of_lane, scale):
+def fold_q(q, k_up, head_of_lane, scale, *, status=None):
     """q [n, H, 128] (RoPE applied), U^T [W, 128] -> A|B [n, W, 128] f16 with the
     logit scale folded in (paged_quant.py:241-255):
 
       A[r,i] = q_i U[r,i] + q_{i+64} U[r,i+64]      B[r,i] = q_{i+64} U[r,i] - q_i U[r,i+64]
-    """
+
+    ``status`` (optional device int32 tensor): a ``head_of_lane`` entry outside
+    ``[0, H)`` gives a zero row and is recorded there as STARKV_EBOUNDS (105)."""
     n, W = q.shape[0], k_up.shape[0]
     assert q.stride(-1) == 1 and k_up.stride(-1) == 1
     ab = torch.empty(n, W, HEAD_DIM, device=q.device, dtype=torch.float16)
@@ -161,7 +163,7 @@ def fold_q(q, k_up, head_of_lane, scale):
     us = (C.c_int64 * 2)(*k_up.stride())
     st = _lib.lib().starkv_fold_q(q.data_ptr(), qs, _lib.dtype_code(q), k_up.data_ptr(), us, _lib.dtype_code(k_up),
                                   head_of_lane.data_ptr(), n, q.shape[1], W, float(scale), ab.data_ptr(),
-                                  _lib.stream_ptr(q.device))
+                                  _lib.ptr(status), _lib.stream_ptr(q.device))
     _lib.check(st, "fold_q")
     return ab
 

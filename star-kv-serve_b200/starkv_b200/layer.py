@@ -42,6 +42,27 @@ class AttnWeights:
     v_rank: int
     num_heads: int
     num_kv_heads: int
+    rotated: bool = False     # K/V factors already in the 3.2-bit cache's rotated basis
+
+    @classmethod
+    def from_checkpoint(cls, lw, wq: torch.Tensor, wo: torch.Tensor, num_heads: int, device=None,
+                        dtype=torch.bfloat16) -> "AttnWeights":
+        """The layer's weights from a fused checkpoint layer (starkv_b200.checkpoint,
+        the serving layout) plus the model's q_proj / o_proj rows, as
+        StarKVAttentionImpl.to_device builds them (attention.py:134-166): kv_down =
+        [k_down | v_down], k_up as stored, and one V up-projection per KV head,
+        repeated over that head's query heads, as v_up_by_q [Hq, rv, Hd]. A checkpoint
+        loaded with kv_quant carries the Hadamard rotations already (rotated=True)."""
+        H = lw.k_head_ranks.numel()
+        if num_heads % H:
+            raise ValueError(f"{num_heads} query heads do not group over {H} KV heads")
+        dev = device if device is not None else wq.device
+        v_up_by_q = (lw.v_up.view(H, HEAD_DIM, lw.v_rank).repeat_interleave(num_heads // H, dim=0)
+                     .transpose(-1, -2))
+        return cls(wq=wq.to(device=dev, dtype=dtype), kv_down=torch.cat([lw.k_down, lw.v_down]).to(dev, dtype),
+                   wo=wo.to(device=dev, dtype=dtype), k_up=lw.k_up.to(dev, dtype).contiguous(),
+                   v_up_by_q=v_up_by_q.to(dev, dtype).contiguous(), k_ranks=[int(r) for r in lw.k_head_ranks],
+                   v_rank=lw.v_rank, num_heads=num_heads, num_kv_heads=H, rotated=lw.kv_quant)
 
 
 def random_weights(hidden: int, num_heads: int, ranks: list[int], v_rank: int, seed: int = 0,
@@ -109,7 +130,8 @@ class StarKVAttentionLayer:
         if quant:
             self.row = pq.QuantRow(W, len(heads), w.v_rank)
             self.k_nouts, self.head_of_lane, self.k_tiles = pq.k_tables(ranks, dev)
-            self._fold_rotations(w.k_ranks, heads, offsets)
+            if not w.rotated:   # a kv_quant checkpoint carries the rotations already
+                self._fold_rotations(w.k_ranks, heads, offsets)
         else:
             self.row = None
         # prefill lifts every head in one bmm over a uniform width: codes gathered
@@ -170,6 +192,9 @@ class StarKVAttentionLayer:
         n = hidden.shape[0]
         q = rope(F.linear(hidden, self.wq).view(n, self.num_heads, HEAD_DIM), positions, self.cos_sin_cache)
         k, v = self.codes(hidden)
+        # CUDA-graph padding rows carry slot -1 (written to the reserved null block)
+        # and length 0; as attention.py:199 does, they attend to one null-block position
+        seq_lens = seq_lens.clamp(min=1)
         if self.quant:
             pq.pack_kv(k, v, cache, slot_mapping, self.row, self.k_ranks, self.k_head_offsets, self.k_nouts)
             attn = pq.paged_quant_decode(q, cache, block_table, seq_lens, max_seq_len, self.row, self.k_up,

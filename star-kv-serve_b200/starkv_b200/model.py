@@ -9,7 +9,9 @@ reference's stock LlamaAttention does). Tensor parallel over `world` ranks in th
 Megatron layout the reference leaves at TP=1 (model.py:32-33): attention heads and
 the MLP's intermediate columns are split, o_proj and down_proj are row-parallel
 and all-reduced; embedding, norms and LM head are replicated. Weights are
-seeded random-init of the configured geometry.
+seeded random-init of the configured geometry; the compressed layers' K/V factors
+can come from a fused_weights.pt instead (starkv_b200.checkpoint), which then
+also decides which layers are compressed.
 
 With attn_parallel="context" the compressed layers split their KV cache by pages
 instead of heads (starkv_b200.layer.StarKVContextLayer): every rank holds all heads
@@ -54,6 +56,12 @@ class ModelConfig:
             v = rng.choice(self.v_rank_choices, size=self.heads, p=self.v_rank_probs)
             self.ranks[i] = ([int(x) for x in k], int(v.sum()))
         return self.ranks[i]
+
+
+def checkpoint_layer_ranks(cfg: ModelConfig) -> dict:
+    """(K ranks, V rank) of every compressed layer of `cfg`, for
+    starkv_b200.checkpoint.write_synthetic_checkpoint."""
+    return {i: cfg.layer_ranks(i) for i in range(cfg.layers) if i not in cfg.full_layers}
 
 
 def _rnd(shape, std, g, device, dtype=torch.bfloat16):
@@ -115,9 +123,24 @@ class StarKVModel:
     """The model on one rank of a tensor-parallel group (world 1: whole)."""
 
     def __init__(self, cfg: ModelConfig, device, quant: bool = False, rank: int = 0, world: int = 1, group=None,
-                 dtype=torch.bfloat16, attn_parallel: str = "heads"):
+                 dtype=torch.bfloat16, attn_parallel: str = "heads", checkpoint=None):
+        """`checkpoint`: a fused_weights.pt (path, state dict or loaded
+        starkv_b200.checkpoint.StarKVCheckpoint) whose compressed layers' K/V factors
+        the model serves; the layers it leaves out are full-rank. Without one, every
+        layer outside cfg.full_layers gets seeded random factors. The other weights
+        (embedding, q/o projections, MLP, norms, LM head) are seeded random-init
+        either way: the checkpoint holds only the K/V factors."""
         if attn_parallel not in ("heads", "context"):
             raise ValueError(f"attn_parallel must be 'heads' or 'context', not {attn_parallel!r}")
+        ckpt = None
+        if checkpoint is not None:
+            import dataclasses
+            from .checkpoint import StarKVCheckpoint, load_fused_checkpoint
+            ckpt = checkpoint if isinstance(checkpoint, StarKVCheckpoint) else load_fused_checkpoint(
+                checkpoint, cfg.layers, cfg.heads, HEAD_DIM, dtype=torch.float32, kv_quant=quant)
+            if any(lw.kv_quant != quant for lw in ckpt.layers.values()):
+                raise ValueError("checkpoint loaded with kv_quant != the model's quant")
+            cfg = dataclasses.replace(cfg, full_layers=tuple(ckpt.skip_layers))
         self.cfg, self.quant, self.rank, self.world, self.group = cfg, quant, rank, world, group
         self.attn_parallel = attn_parallel
         self.device = torch.device(device)
@@ -141,6 +164,11 @@ class StarKVModel:
                 wv = _rnd((H * HEAD_DIM, d), d ** -0.5, gl, self.device, dtype)
                 attn = StockAttentionLayer(wq, wk, wv, wo, self.cos_sin_cache, rank, world, group)
                 del wk, wv
+            elif ckpt is not None:
+                w = AttnWeights.from_checkpoint(ckpt.layers[i], wq, wo, H, device=self.device, dtype=dtype)
+                attn = (StarKVContextLayer if attn_parallel == "context" else StarKVAttentionLayer)(
+                    w, self.cos_sin_cache, quant=quant, rank=rank, world=world, group=group)
+                del w
             else:
                 ranks, rv = cfg.layer_ranks(i)
                 offs = sharding.k_offsets(ranks)

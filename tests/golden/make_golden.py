@@ -18,7 +18,11 @@ Every expected value below is produced by the reference's own code:
 * 3.2-bit decode: ``kv_quant.unpack_k_ref`` / ``unpack_v_ref`` followed by the same
   math, plus ``paged_quant_decode`` (paged_quant.py:357-411) under the interpreter;
 * weights layout: ``starkv_serve.checkpoint._load_layer`` (checkpoint.py:106-169)
-  for a small synthetic fused state dict, with and without ``kv_quant``.
+  for a small synthetic fused state dict, with and without ``kv_quant``, and
+  ``load_fused_checkpoint`` (checkpoint.py:74-93) on a small fused_weights.pt
+  with compressed and uncompressed layers;
+* query fold: ``starkv_serve.kernels.paged_quant.fold_q`` (paged_quant.py:223-255)
+  under Triton's CPU interpreter.
 
 The fixtures are small .npz files; bf16 tensors are stored as uint16 bits.
 """
@@ -308,6 +312,25 @@ def make_ckpt_case():
     return out
 
 
+def make_fold_case():
+    g = torch.Generator().manual_seed(13)
+    ranks = [16, 20, 37, 64, 5]
+    widths = [align16(r) for r in ranks]
+    offsets = [sum(widths[:h]) for h in range(len(ranks))]
+    W = sum(widths)
+    H, n = len(ranks), 3
+    _, hol, _ = ref_pq.k_tables(ranks, "cpu")
+    q = torch.randn(n, H, 128, generator=g).to(torch.bfloat16)
+    k_up = torch.zeros(W, 128)
+    for r, o in zip(ranks, offsets):
+        k_up[o:o + r] = torch.randn(r, 128, generator=g) / r ** 0.5
+    k_up = k_up.to(torch.bfloat16)
+    scale = 128 ** -0.5
+    ab = ref_pq.fold_q(q.float(), k_up.float(), hol, scale)        # fp32 inputs (bf16 values)
+    return dict(query=bits(q), k_up=bits(k_up), head_of_lane=hol.numpy(), scale=np.float32(scale),
+                ab_f16=ab.numpy())
+
+
 def main():
     for name, case in make_pack_cases().items():
         np.savez_compressed(os.path.join(OUT, f"pack_{name}.npz"), **case)
@@ -322,6 +345,7 @@ def main():
     np.savez_compressed(os.path.join(OUT, "decode_quant_b.npz"),
                         **make_quant_case("quant_b", [64, 48, 5, 128], 160, [16, 31, 130], 5))
     np.savez_compressed(os.path.join(OUT, "checkpoint_layer.npz"), **make_ckpt_case())
+    np.savez_compressed(os.path.join(OUT, "fold_q.npz"), **make_fold_case())
     print("golden fixtures written to", OUT)
 
 

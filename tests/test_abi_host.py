@@ -81,6 +81,14 @@ def test_entry_points_reject_bad_arguments_before_any_gpu_work(lib):
     a = _lib.DecodeArgs()
     a.n, a.num_heads, a.num_kv_heads, a.k_width, a.v_rank, a.max_seq_len = 64, 32, 32, 1392, 1536, 8192
     assert lib.starkv_paged_decode_bf16_noalloc(C.byref(a), None) == 102   # larger than its scratch
+    assert lib.starkv_noalloc_read_status(None, 0, None) == 22
+    # fold_q: element types and the lane count are checked before any GPU work
+    qs, us = _lib.i64s([4096, 128, 1]), _lib.i64s([128, 1])
+    fake = C.c_void_p(4096)   # never dereferenced: every call below is refused first
+    assert lib.starkv_fold_q(fake, qs, _lib.U8, fake, us, _lib.BF16, fake, 2, 32, 64, 0.1, fake, None, None) == 101
+    assert lib.starkv_fold_q(fake, qs, _lib.BF16, fake, us, 9, fake, 2, 32, 64, 0.1, fake, None, None) == 101
+    assert lib.starkv_fold_q(fake, qs, _lib.BF16, fake, us, _lib.BF16, fake, 2, 32, 40, 0.1, fake, None, None) == 22
+    assert lib.starkv_fold_q(None, qs, _lib.BF16, fake, us, _lib.BF16, fake, 2, 32, 64, 0.1, fake, None, None) == 22
 
 
 def test_quant_row_matches_oracle():

@@ -170,3 +170,44 @@ def test_two_rank_page_split_matches_unsplit_decode():
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         assert result["scale"] > 0
         assert result["err"] <= 1e-10 * max(1.0, result["scale"]), result["err"]
+
+
+def _agree_rank_main(rank, port, result):
+    """Rank 1 has fewer cache blocks than rank 0: extend_agreed refuses on both
+    ranks, neither table moves, and after a release both extend together."""
+    from starkv_b200 import context_parallel as cp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        t = cp.PageSplitTables(rank, WORLD, 64 if rank == 0 else 3)
+        cp.extend_agreed(t, "a", 48)
+        cp.extend_agreed(t, "b", 40)
+        before = (dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free))
+        refused = False
+        try:
+            cp.extend_agreed(t, "a", 32)          # rank 1 is out of blocks
+        except RuntimeError:
+            refused = True
+        same = before == (dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free))
+        t.release("b")
+        slots = cp.extend_agreed(t, "a", 32)
+        result[rank] = (refused, same, t.lens["a"], sum(s >= 0 for s in slots))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_page_split_extension_is_agreed_by_all_ranks():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        result = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_agree_rank_main, args=(r, port, result)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        res = dict(result)
+    assert all(res[r][0] and res[r][1] for r in range(WORLD))      # both refused, nothing changed
+    assert [res[r][2] for r in range(WORLD)] == [80, 80]             # both grew together afterwards
+    assert res[0][3] + res[1][3] == 32                               # each new token on exactly one rank

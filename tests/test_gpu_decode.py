@@ -94,29 +94,32 @@ def test_quant_decode_golden(golden_dir, name):
 
 
 def _oracle_bf16(layer, seqs):
+    from oracle_pool import oracle_map
+    from starkv_b200.workload import gather_rows
     f = lambda t: t.float().cpu().numpy()  # noqa: E731
-    outs = []
-    for b in seqs:
-        from starkv_b200.workload import gather_rows
-        rows = gather_rows(layer, b).float().numpy()
-        outs.append(O.attend_one(f(layer.query[b]), rows[:, :layer.k_width], rows[:, layer.k_width:],
-                                 f(layer.k_up), layer.ranks, layer.offsets,
-                                 layer.num_heads // len(layer.ranks), f(layer.v_up_by_q), f(layer.cos_sin_cache),
-                                 layer.scale))
-    return np.stack(outs)
+    k_up, v_up, cs, q = f(layer.k_up), f(layer.v_up_by_q), f(layer.cos_sin_cache), f(layer.query)
+    rows = {b: gather_rows(layer, b).float().numpy() for b in seqs}   # device reads stay on this thread
+
+    def one(b):
+        r = rows[b]
+        return O.attend_one(q[b], r[:, :layer.k_width], r[:, layer.k_width:], k_up, layer.ranks, layer.offsets,
+                            layer.num_heads // len(layer.ranks), v_up, cs, layer.scale, dtype=np.float32)
+    return np.stack(oracle_map(one, seqs))
 
 
 def _oracle_quant(layer, seqs):
+    from oracle_pool import oracle_map
     from starkv_b200.workload import gather_rows
     f = lambda t: t.float().cpu().numpy()  # noqa: E731
     row = O.QuantRow(layer.k_width, len(layer.ranks), layer.v_rank)
-    outs = []
-    for b in seqs:
-        rows = gather_rows(layer, b).numpy()
-        kd, vd = O.unpack_rows(rows, row, layer.ranks)
-        outs.append(O.attend_one(f(layer.query[b]), kd, vd, f(layer.k_up), layer.ranks, layer.offsets, 1,
-                                 f(layer.v_up_by_q), f(layer.cos_sin_cache), layer.scale))
-    return np.stack(outs)
+    k_up, v_up, cs, q = f(layer.k_up), f(layer.v_up_by_q), f(layer.cos_sin_cache), f(layer.query)
+    rows = {b: gather_rows(layer, b).numpy() for b in seqs}
+
+    def one(b):
+        kd, vd = O.unpack_rows(rows[b], row, layer.ranks)
+        return O.attend_one(q[b], kd, vd, k_up, layer.ranks, layer.offsets, 1, v_up, cs, layer.scale,
+                            dtype=np.float32)
+    return np.stack(oracle_map(one, seqs))
 
 
 EDGE_LENS = [1, 15, 16, 17, 127, 128, 129, 300, 1000, 2049]
@@ -177,9 +180,9 @@ def test_quant_pack_matches_oracle_bits():
 
 
 @pytest.mark.parametrize("quant", [False, True])
-def test_full_size_config_sampled(quant):
-    """Configs 2/3 at full size; every sequence checked by a size-independent
-    property (finite, bounded by the V lift), three sampled sequences by the oracle."""
+def test_full_size_config_every_sequence(quant):
+    """Configs 2/3 at full size (64 x 8192 bf16, 64 x 16384 3.2-bit): every one of
+    the 64 sequences against the float32 oracle."""
     from starkv_b200.kernels import paged_quant as pq
     from starkv_b200.kernels.paged_decode import paged_starkv_decode
     from starkv_b200.workload import make_layer
@@ -189,16 +192,98 @@ def test_full_size_config_sampled(quant):
     if quant:
         out = pq.paged_quant_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.row, L.k_up,
                                     L.head_of_lane, L.k_tiles, L.v_up_by_q, L.cos_sin_cache, L.scale)
-        ref = _oracle_quant(L, [0, 31, 63])
+        ref = _oracle_quant(L, range(n))
     else:
         out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
                                   L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale)
-        ref = _oracle_bf16(L, [0, 31, 63])
+        ref = _oracle_bf16(L, range(n))
     o = out.float().cpu().numpy()
     assert np.isfinite(o).all()
-    assert_close(o[[0, 31, 63]], ref)
+    assert_close(o, ref)
     del L
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_config4_mixed_lengths_skewed_ranks(quant):
+    """Config 4's geometry: 256 sequences with contexts seeded uniform in [1024,
+    32768] (4.3 M tokens), skewed per-head ranks (K 16..128, V 32..128 per head),
+    32 heads. Every output finite; 24 sequences against the float32 oracle: the
+    shortest, the longest and 22 seeded picks."""
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer, sample_ranks
+    dev = cuda()
+    rng = np.random.default_rng(4)
+    lens = [int(x) for x in rng.integers(1024, 32768 + 1, size=256)]
+    ranks, rv = sample_ranks(32, 4, skewed=True)
+    ranks[5] = 128                       # the sampler's top K rank (this seed draws up to 96)
+    assert rv > 32 * 32
+    L = make_layer(lens, num_heads=32, quant=quant, seed=4, device=dev, ranks=ranks, v_rank=rv)
+    picks = sorted({int(np.argmin(lens)), int(np.argmax(lens)), *rng.choice(256, 22, replace=False).tolist()})
+    if quant:
+        out = pq.paged_quant_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.row, L.k_up,
+                                    L.head_of_lane, L.k_tiles, L.v_up_by_q, L.cos_sin_cache, L.scale)
+        ref = _oracle_quant(L, picks)
+    else:
+        out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up, L.k_ranks,
+                                  L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale)
+        ref = _oracle_bf16(L, picks)
+    o = out.float().cpu().numpy()
+    assert np.isfinite(o).all()
+    assert_close(o[picks], ref)
+    del L
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_zero_length_rows_give_zero_output(quant):
+    """A row with seq_len 0 (a padding row the caller did not clamp, attention.py:199
+    does) attends to nothing: its output is exactly zero, never NaN, and the other
+    rows are unaffected. (The reference's softmax over an all -inf row gives NaN;
+    its caller clamps the length to 1, which the layer here does too.)"""
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer
+    dev = cuda()
+    L = make_layer([300, 1, 40], num_heads=32, quant=quant, seed=8, device=dev)
+    sl = L.seq_lens.clone()
+    sl[1] = 0
+    if quant:
+        out = pq.paged_quant_decode(L.query, L.kv_cache, L.block_table, sl, L.max_seq_len, L.row, L.k_up,
+                                    L.head_of_lane, L.k_tiles, L.v_up_by_q, L.cos_sin_cache, L.scale)
+        ref = _oracle_quant(L, [0, 2])
+    else:
+        out = paged_starkv_decode(L.query, L.kv_cache, L.block_table, sl, L.max_seq_len, L.k_up, L.k_ranks,
+                                  L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache, L.scale)
+        ref = _oracle_bf16(L, [0, 2])
+    o = out.float().cpu().numpy()
+    assert np.all(o[1] == 0)
+    assert_close(o[[0, 2]], ref)
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_repeated_calls_agree_within_f32_rounding(quant):
+    """P.V partial sums from CTAs that share a sequence meet in f32 atomic adds, whose
+    order varies between runs, so two identical calls may differ in the last bits of
+    the f32 sums (not bit-identical). They agree to far inside the tolerance."""
+    from starkv_b200.kernels import paged_quant as pq
+    from starkv_b200.kernels.paged_decode import paged_starkv_decode
+    from starkv_b200.workload import make_layer
+    dev = cuda()
+    L = make_layer([5000, 3000, 7000], num_heads=32, quant=quant, seed=9, device=dev)
+    outs = []
+    for _ in range(3):
+        if quant:
+            outs.append(pq.paged_quant_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.row,
+                                              L.k_up, L.head_of_lane, L.k_tiles, L.v_up_by_q, L.cos_sin_cache,
+                                              L.scale).float())
+        else:
+            outs.append(paged_starkv_decode(L.query, L.kv_cache, L.block_table, L.seq_lens, L.max_seq_len, L.k_up,
+                                            L.k_ranks, L.k_head_offsets, L.k_width, L.v_up_by_q, L.cos_sin_cache,
+                                            L.scale).float())
+    for o in outs[1:]:
+        assert torch.allclose(o, outs[0], atol=1e-3, rtol=1e-3)
 
 
 def test_bad_block_id_recorded_not_faulting():

@@ -113,6 +113,45 @@ def test_layer_decode_step_vs_oracle(quant):
 
 
 @pytest.mark.parametrize("quant", [False, True])
+def test_layer_decode_step_with_padding_rows(quant):
+    """A CUDA-graph padded batch (attention.py:181, 199): two padding rows with slot
+    -1, length 0 and an all-zero block table row ride along with the real rows. They
+    write their codes to the reserved null block (slot -1 -> block 0, position 0),
+    attend to that one position (length clamped to 1) and give a finite output equal
+    to the oracle's over the row that landed there; the real rows are unchanged."""
+    from starkv_b200.layer import rope
+    layers, caches, bt, seq_lens, new, positions, slots = setup(quant)
+    ly, cache = layers[0], caches[0]
+    dev, n, P = new.device, len(LENS), 2
+    g = torch.Generator(device=dev).manual_seed(99)
+    pad_hidden = torch.randn(P, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+    out = ly.forward(torch.cat([new, pad_hidden]), torch.cat([positions, torch.zeros(P, dtype=positions.dtype,
+                                                                                     device=dev)]),
+                     cache, torch.cat([bt, torch.zeros(P, bt.shape[1], dtype=bt.dtype, device=dev)]),
+                     torch.cat([seq_lens, torch.zeros(P, dtype=seq_lens.dtype, device=dev)]), max(LENS),
+                     torch.cat([slots, torch.full((P,), -1, dtype=slots.dtype, device=dev)]))
+    got = out.double().cpu().numpy()
+    assert np.isfinite(got).all()
+    ref = reference(ly, cache, bt, new, positions)
+    assert np.all(np.abs(got[:n] - ref) <= 2e-2 + 1e-2 * np.abs(ref))
+    # padding rows: the oracle over the single null-block position 0, whatever row landed there
+    f = lambda t: t.double().cpu().numpy()  # noqa: E731
+    rows = cache[0, :1].cpu()
+    if quant:
+        kd, vd = O.unpack_rows(rows.numpy(), O.QuantRow(ly.k_width, ly.num_kv_heads, ly.v_rank), ly.k_ranks_host)
+    else:
+        r = rows.double().numpy()
+        kd, vd = r[:, :ly.k_width], r[:, ly.k_width:]
+    qp = rope(torch.nn.functional.linear(pad_hidden, ly.wq).view(P, ly.num_heads, 128),
+              torch.zeros(P, dtype=torch.long, device=dev), ly.cos_sin_cache)
+    for i in range(P):
+        a = O.attend_one(f(qp[i]), kd, vd, f(ly.k_up), ly.k_ranks_host, ly.k_head_offsets.tolist(),
+                         ly.num_heads // ly.num_kv_heads, f(ly.v_up_by_q), f(ly.cos_sin_cache), ly.scale)
+        refp = a.reshape(-1) @ f(ly.wo).T
+        assert np.all(np.abs(got[n + i] - refp) <= 2e-2 + 1e-2 * np.abs(refp))
+
+
+@pytest.mark.parametrize("quant", [False, True])
 def test_layer_head_shards_sum_to_whole(quant):
     """Two head shards (LPT) on one GPU: their o_proj partial sums add up to the
     whole layer's output (the all-reduce of a 2-rank group)."""

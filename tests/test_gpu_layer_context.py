@@ -164,15 +164,17 @@ def test_page_split_prefill_then_decode(quant):
 
 @pytest.mark.parametrize("quant", [False, True])
 def test_page_split_tables_drive_prefill_and_growing_decode(quant):
-    """Two emulated ranks, each with a context_parallel.PageSplitTables, prefill two
+    """Two emulated ranks, each with a context_parallel.PageSplitTables, prefill three
     prompts and then decode 24 steps. The steps cross page boundaries, so ownership of
-    the new token alternates between the ranks. Every step's combined output matches
-    the whole layer's step."""
+    the new token alternates between the ranks. The 5-token prompt fits in page 0, so
+    rank 1 starts with no token of that sequence (an empty block-table row, length 0,
+    a partial with max -inf) and takes its first page at position 16 during the
+    decode. Every step's combined output matches the whole layer's step."""
     from starkv_b200 import context_parallel as cp
     from starkv_b200 import layer as Ly
     from starkv_b200.workload import rope_cos_sin, sample_ranks
     dev = cuda()
-    world, P, steps = 2, [20, 45], 24
+    world, P, steps = 2, [5, 20, 45], 24
     ranks, rv = sample_ranks(HEADS, 7)
     w = Ly.random_weights(HIDDEN, HEADS, ranks, rv, seed=7, device=dev)
     cs = rope_cos_sin(1024, dev)
@@ -194,6 +196,7 @@ def test_page_split_tables_drive_prefill_and_growing_decode(quant):
     for ly, tab, cache in zip(lys, tabs, caches):
         ly.prefill(prompt, ppos, P, cache, slots_of(tab, P))
     lens = list(P)
+    assert tabs[1].local_len(0) == 0                    # rank 1 holds nothing of the short prompt yet
     for step in range(steps):
         new = torch.randn(len(P), HIDDEN, generator=g, device=dev).to(torch.bfloat16)
         pos = torch.tensor(lens, device=dev)
@@ -210,3 +213,4 @@ def test_page_split_tables_drive_prefill_and_growing_decode(quant):
         err = (got - ref).abs()
         assert bool((err <= 2e-2 + 1e-2 * ref.abs()).all()), f"step {step}: max abs err {float(err.max()):.3e}"
         lens = [L + 1 for L in lens]
+    assert tabs[1].local_len(0) == lens[0] - 16         # ...and took its first page during the decode

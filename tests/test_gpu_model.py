@@ -88,3 +88,30 @@ def test_model_decode_matches_dense_reference():
     assert float(rel) < 3e-2, f"relative error {float(rel):.3e}"
     agree = (logits.argmax(-1) == ref.argmax(-1)).float().mean()
     assert float(agree) >= 2 / 3
+
+
+def test_model_from_fused_checkpoint_file(tmp_path):
+    """The model served from a fused_weights.pt written in the reference layout
+    (random-init factors, one layer left out and so full-rank): the loader's layout
+    reaches the kernels, and decoding matches the dense recomputation."""
+    from starkv_b200.checkpoint import write_synthetic_checkpoint
+    from starkv_b200.model import StarKVModel, checkpoint_layer_ranks
+    dev = cuda()
+    cfg = small_config()
+    path = tmp_path / "fused_weights.pt"
+    write_synthetic_checkpoint(str(path), checkpoint_layer_ranks(cfg), cfg.hidden, cfg.heads, seed=2)
+    model = StarKVModel(small_config(), dev, checkpoint=str(path))
+    assert [ly["full"] for ly in model.layers] == [True, False, False]
+    g = torch.Generator(device=dev).manual_seed(3)
+    tokens = torch.randint(0, model.cfg.vocab, (BATCH, STEPS), generator=g, device=dev)
+    pages = -(-STEPS // 16)
+    caches = model.allocate_caches(BATCH * pages + 1)
+    bt = (torch.arange(BATCH * pages, device=dev, dtype=torch.int32).view(BATCH, pages) + 1)
+    for t in range(STEPS):
+        pos = torch.full((BATCH,), t, device=dev)
+        slots = bt[:, t // 16].long() * 16 + t % 16
+        seq_lens = torch.full((BATCH,), t + 1, dtype=torch.int32, device=dev)
+        logits = model.decode_step(tokens[:, t], pos, caches, bt, seq_lens, STEPS, slots)
+    ref = dense_reference(model, tokens)
+    rel = (logits - ref).norm() / ref.norm()
+    assert float(rel) < 3e-2, f"relative error {float(rel):.3e}"

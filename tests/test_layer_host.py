@@ -138,8 +138,9 @@ def test_page_split_tables_place_growing_sequences(world):
     import numpy as np
     from starkv_b200 import context_parallel as cp
     rng = random.Random(world)
-    nb = 64
+    nb = 2 + 16 // world                 # small enough that ranks run short during the walk
     tabs = [cp.PageSplitTables(r, world, nb) for r in range(world)]
+    refused = 0
     caches = [np.full((nb, 16), -1, dtype=np.int64) for _ in range(world)]   # global position stored per slot
     live, next_id = {}, 0
     for step in range(300):
@@ -158,9 +159,11 @@ def test_page_split_tables_place_growing_sequences(world):
         else:
             continue
         try:
-            slots = [t.extend(sid, n) for t in tabs]
+            slots = cp.extend_on_all_ranks(tabs, sid, n)
         except RuntimeError:
-            continue                      # a rank is full; the tables are unchanged
+            refused += 1
+            assert all(t.lens.get(sid, 0) == live[sid] for t in tabs)   # no rank moved
+            continue                      # a rank is short: no rank extended
         L0 = live[sid]
         for i in range(n):
             owners = [r for r in range(world) if slots[r][i] >= 0]
@@ -182,6 +185,7 @@ def test_page_split_tables_place_growing_sequences(world):
             held = [b for s in ids for b in t.blocks.get(s, [])]
             assert len(held) == len(set(held)) and 0 not in held      # no block twice, null block kept
             assert len(held) + len(t.free) == nb - 1                  # freed blocks go back to the pool
+    assert refused > 0                    # the refusal path ran
     # a refused extension leaves the tables as they were
     t = cp.PageSplitTables(0, world, 3)
     t.extend("a", 16)
@@ -189,3 +193,24 @@ def test_page_split_tables_place_growing_sequences(world):
     with pytest.raises(RuntimeError):
         t.extend("a", 16 * world * 4)
     assert before == (dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free))
+
+
+def test_page_split_refusal_keeps_all_ranks_consistent():
+    """Rank 1 is short of blocks while rank 0 is not: the group refuses as a whole,
+    every rank keeps its lengths and its pool intact, and the sequence can still grow
+    once rank 1 frees blocks."""
+    from starkv_b200 import context_parallel as cp
+    tabs = [cp.PageSplitTables(0, 2, 64), cp.PageSplitTables(1, 2, 3)]   # rank 1: 2 usable blocks
+    cp.extend_on_all_ranks(tabs, "a", 48)            # pages 0, 2 on rank 0; page 1 on rank 1
+    cp.extend_on_all_ranks(tabs, "b", 40)            # rank 1 takes its second (last) block
+    assert not tabs[1].free and tabs[1].blocks_needed("a", 32) == 1
+    assert tabs[0].can_extend("a", 32) and not tabs[1].can_extend("a", 32)
+    before = [(dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free)) for t in tabs]
+    with pytest.raises(RuntimeError):
+        cp.extend_on_all_ranks(tabs, "a", 32)
+    assert before == [(dict(t.lens), {k: list(v) for k, v in t.blocks.items()}, list(t.free)) for t in tabs]
+    for t in tabs:
+        t.release("b")
+    slots = cp.extend_on_all_ranks(tabs, "a", 32)
+    assert [t.lens["a"] for t in tabs] == [80, 80]
+    assert sum(s >= 0 for s in slots[0]) + sum(s >= 0 for s in slots[1]) == 32

@@ -85,3 +85,18 @@ def test_quantizer_ties_round_half_even():
     n, s = O.quantize_block(np.zeros((1, 5), np.float32), 3)
     assert s[0] == np.float32(1e-5) / np.float32(3)
     assert (n == 8).all()
+
+
+def test_fold_q_matches_reference_fixture(golden_dir):
+    """The oracle's fold_q against the reference's own fold_q (paged_quant.py:223-255,
+    run by Triton's CPU interpreter): equal to within one float16 ulp (the two may
+    fuse one multiply-add differently)."""
+    c = load(golden_dir, "fold_q.npz")
+    f = O.bf16_bits_to_f32
+    ab = O.fold_q(f(c["query"]), f(c["k_up"]), c["head_of_lane"], float(c["scale"]))
+    ref = c["ab_f16"]
+    assert ab.shape == ref.shape
+    d = np.abs(ab.astype(np.float32) - ref.astype(np.float32))
+    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
+    assert np.all(d <= ulp), f"max diff {d.max()}"
+    assert (d == 0).mean() > 0.99

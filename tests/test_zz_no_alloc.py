@@ -6,8 +6,12 @@ this library owns every allocation): it runs in a scratch array built into the
 library instead of a caller workspace. These tests check that two calls in a
 row agree with the workspace entry point (starkv_paged_decode_bf16) on the same
 inputs, within the decode tolerance used everywhere else (2e-2 abs + 1e-2 rel),
-and that a call too large for the built-in scratch is refused before any GPU
-work. This file is named to be collected last.
+that a call too large for the built-in scratch is refused before any GPU work,
+and that device-side errors recorded in the built-in scratch reach the caller
+through starkv_noalloc_read_status. The workspace entry point is the reference
+here because its own tests pin it to the oracle (tests/test_gpu_decode.py);
+agreeing with it within the tolerance is agreeing with the oracle. This file
+is named to be collected last.
 """
 import ctypes as C
 
@@ -90,3 +94,30 @@ def test_noalloc_refuses_calls_larger_than_its_scratch():
     st = lib.starkv_paged_decode_bf16_noalloc(a, _lib.stream_ptr(dev))
     assert st == 102   # STARKV_EWORKSPACE
     assert not out.any()
+
+
+def test_noalloc_reports_device_errors_through_its_status_word():
+    """A block id outside the cache is skipped by the kernels and recorded in the
+    built-in scratch's status word; the caller reads it with
+    starkv_noalloc_read_status, and the next call starts from a clear word."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from starkv_b200 import _lib
+    from starkv_b200.workload import make_layer
+    dev = torch.device("cuda", 0)
+    lib = _lib.lib()
+    layer = make_layer([40, 40], num_heads=32, seed=24, device=dev)
+    good_bt = layer.block_table
+    layer.block_table = good_bt.clone()
+    layer.block_table[1, 1] = layer.kv_cache.shape[0] + 1000   # outside the cache
+    out = torch.zeros(layer.n, 32, 128, dtype=torch.bfloat16, device=dev)
+    st = lib.starkv_paged_decode_bf16_noalloc(_args(layer, out), _lib.stream_ptr(dev))
+    assert st == 0, lib.starkv_strerror(st)
+    word = _lib.i32(0)
+    assert lib.starkv_noalloc_read_status(C.byref(word), 0, _lib.stream_ptr(dev)) == 0
+    assert word.value == 105   # STARKV_EBOUNDS
+    layer.block_table = good_bt
+    st = lib.starkv_paged_decode_bf16_noalloc(_args(layer, out), _lib.stream_ptr(dev))
+    assert st == 0, lib.starkv_strerror(st)
+    assert lib.starkv_noalloc_read_status(C.byref(word), 1, _lib.stream_ptr(dev)) == 0
+    assert word.value == 0
