@@ -10,20 +10,26 @@ reported under "q32". Inputs are seeded synthetic tensors with the configs'
 shapes and distributions (starkv_b200.workload); every step reads a >2 GB cache,
 far larger than the 126 MB L2, so no flush is needed between steps.
 
-N > 1 (torchrun), --parallel seqs (default): the decode sequences are independent,
-so every GPU decodes its own batch of configuration 2 (64 sequences; global batch
-64 N) with no collective on the path; `value` is the whole job's decode tokens per
-second (weak scaling: the work per GPU is fixed). Two strong-scaling splits of the
-one 64-sequence batch are kept for study: --parallel context, every rank decodes all
-heads over its share of each sequence's 256-token tiles and the partials are
-combined exactly with one NCCL all-gather and a native kernel
-(starkv_b200.context_parallel), each GPU reading 1/N of the K and V codes; and
---parallel heads, heads sharded tensor-parallel (LPT on K width) with the V codes
-replicated on every rank (the shared latent is read by every head). The step time is
-always the max over ranks.
+Every default run also measures, in the same line: config 4 (256 mixed-length
+sequences, skewed ranks, both formats: "c4"), config 5 (the whole 32-layer model's
+decode step in a CUDA graph, K/V factors loaded from a synthetic fused_weights.pt:
+"model") and, on one GPU, the reference's own Triton decode on the same inputs
+("gpu_bar"). --skip heads,c4,model,bar leaves parts out.
 
---impl reference: the reference algorithm's CPU restatement (oracle/), timed on
-this host's cores on a bounded sample of the same workload.
+N > 1 (torchrun), --parallel context (default): the one 64-sequence batch is split
+over the GPUs (strong scaling): every rank decodes all heads over its share of each
+sequence's 256-token tiles, and the partials are combined exactly with one NCCL
+all-gather and a native kernel (starkv_b200.context_parallel); each GPU reads 1/N
+of the K and V codes. Beside it the line reports "heads": the same batch with heads
+sharded tensor-parallel (LPT on K width), the north star's split, which keeps the V
+codes whole on every rank (the shared latent is read by every head) and so scales
+sub-linearly. --parallel seqs gives every GPU its own batch of 64 sequences with no
+collective (weak scaling). The step time is always the max over ranks.
+
+--impl reference: the reference's own PyTorch CPU decode math (model.py, imported
+from the installed reference in baseline/_ref; the numpy restatement in oracle/
+when it is not installed), timed on this host's cores on a bounded sample of the
+same workload.
 """
 from __future__ import annotations
 
@@ -345,16 +351,49 @@ def model_case(args, device, world, rank, dist_on):
     of heads (page p of a sequence on rank p % N; every rank decodes all heads over its
     pages, and the partials are all-gathered and combined exactly). The step is captured
     in a CUDA graph when capture works, else run eagerly."""
+    line = model_measure(args, device, world, rank, dist_on, args.parallel, args.batch, args.context)
+    if rank == 0:
+        print(json.dumps({"case": "model", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, **line}),
+              flush=True)
+
+
+def synthetic_checkpoint_path(cfg, dist_on, rank):
+    """Write config 5's random-init fused_weights.pt (the reference layout,
+    starkv_b200.checkpoint) once per job into a temporary folder; every rank then
+    loads it. Returns the path (the caller removes it after loading)."""
+    import tempfile
+    import torch.distributed as dist
+    from starkv_b200.checkpoint import write_synthetic_checkpoint
+    from starkv_b200.model import checkpoint_layer_ranks
+    port = os.environ.get("MASTER_PORT", "single")
+    path = os.path.join(tempfile.gettempdir(), f"starkv_config5_fused_weights_{port}_{os.getuid()}.pt")
+    if rank == 0:
+        write_synthetic_checkpoint(path, checkpoint_layer_ranks(cfg), cfg.hidden, cfg.heads, seed=cfg.seed)
+    if dist_on:
+        dist.barrier()
+    return path
+
+
+def model_measure(args, device, world, rank, dist_on, parallel, batch=None, context=None):
+    """Config 5 decode step (see model_case); returns the measurement as a dict."""
     import torch
     import torch.distributed as dist
     from starkv_b200 import context_parallel as cp
     from starkv_b200.model import ModelConfig, StarKVModel
-    C = args.context or 32768
-    split = "context" if dist_on and args.parallel == "context" else "heads"
+    C = context or 32768
+    split = "context" if dist_on and parallel == "context" else "heads"
     cfg = ModelConfig(max_pos=C)
+    ckpt = None
+    if args.model_weights == "checkpoint":
+        ckpt = synthetic_checkpoint_path(cfg, dist_on, rank)
     model = StarKVModel(cfg, device, quant=False, rank=rank if dist_on else 0, world=world if dist_on else 1,
-                        group=None, attn_parallel=split)
-    if args.batch:
+                        group=None, attn_parallel=split, checkpoint=ckpt)
+    if ckpt is not None:
+        if dist_on:
+            dist.barrier()
+        if rank == 0:
+            os.remove(ckpt)
+    if batch:
         n = args.batch
     else:
         free = torch.cuda.mem_get_info(device)[0]
@@ -431,18 +470,18 @@ def model_case(args, device, world, rank, dist_on):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     kv_gb = sum(sum(t.numel() * t.element_size() for t in (c if isinstance(c, tuple) else (c,))) for c in caches) / 1e9
-    if rank == 0:
-        print(json.dumps({"case": "model", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                          "workload": "config5: 32-layer Llama-2-7B geometry (hidden 4096, FFN 11008, vocab "
-                                      "32000), layers 0,1,2,31 full-rank bf16 KV, 28 STAR-KV bf16 layers",
-                          "sessions": n, "context": C, "parallelism": f"tp{world}" if dist_on else "single",
-                          "compressed_attention_split": "pages (context parallel)" if split == "context"
-                          else "heads",
-                          "mode": mode, "ms_per_step": round(ms, 3), "value": round(n / (ms * 1e-3), 1),
-                          "unit": "decode tok/s (whole model)", "kv_cache_gb_per_gpu": round(kv_gb, 1),
-                          "data": "synthetic (seeded random-init weights and caches)"}), flush=True)
     del graph, model, caches
     torch.cuda.empty_cache()
+    return {"workload": "config5: 32-layer Llama-2-7B geometry (hidden 4096, FFN 11008, vocab 32000), layers "
+                        "0,1,2,31 full-rank bf16 KV, 28 STAR-KV bf16 layers at comp-ratio 0.75",
+            "weights": ("K/V factors from a synthetic fused_weights.pt (reference layout, random init) through "
+                        "starkv_b200.checkpoint; other weights seeded random-init" if ckpt is not None
+                        else "seeded random-init"),
+            "sessions": n, "context": C, "parallelism": f"tp{world}" if dist_on else "single",
+            "compressed_attention_split": "pages (context parallel)" if split == "context" else "heads",
+            "mode": mode, "ms_per_step": round(ms, 3), "value": round(n / (ms * 1e-3), 1),
+            "unit": "decode tok/s (whole model)", "kv_cache_gb_per_gpu": round(kv_gb, 1),
+            "data": "synthetic (seeded caches)"}
 
 
 def rank_tokens(layer, cp):
@@ -545,6 +584,102 @@ def triton_bar(layer, device, steps, ours_decode_ms, ours_out=None):
     return res
 
 
+def reference_torch_decode():
+    """The reference's own PyTorch CPU decode math, imported unmodified from the
+    installed reference (baseline/_ref): model._expand_ragged_k (model.py:1204-1220),
+    model._rope_tables (model.py:127-137) and transformers' rotate_half, composed
+    as the no-Triton decode branch does (model.py:1333-1386): expand K per head
+    from its rank, rotate it, q.K^T * scale, softmax in the cache dtype, P.V over
+    the shared V codes, bmm lift per query head. None when not importable."""
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import torch
+        import torch.nn.functional as F
+        import model as ref_model
+    except Exception:   # noqa: BLE001 - the numpy port is the fallback
+        return None
+
+    def decode(q, key_states, value_states, k_up, segments, u_by_q, inv_freq, scale):
+        # q [B, Hq, 1, Hd]; key_states rank-major [B, W, L]; value_states [B, L, rv]
+        key_full = ref_model._expand_ragged_k(key_states, k_up, segments)
+        k_cos, k_sin = ref_model._rope_tables(inv_freq, key_full.shape[-2], key_full.device, key_full.dtype)
+        key_full = key_full * k_cos + ref_model.rotate_half(key_full) * k_sin
+        attn = torch.matmul(q, key_full.transpose(2, 3)) * scale
+        attn = F.softmax(attn, dim=-1).to(q.dtype)
+        prob_v = attn.squeeze(2) @ value_states
+        return torch.bmm(prob_v.transpose(0, 1), u_by_q).transpose(0, 1)
+    return decode
+
+
+def reference_cpu_time(batch, L, dtype_name, seconds=10.0, reps_min=3):
+    """Time the reference's CPU decode (reference_torch_decode) on `batch` sequences
+    of `L` tokens (contiguous cache, config-1 sampling: K ranks {16,32,48,64}, V
+    {32,64} per head, codes and q ~ N(0,1), B_k / B_v ~ N(0, 1/sqrt(rank))) with
+    all host threads. Returns (sequences per second, ms per call) or None."""
+    import torch
+    dec = reference_torch_decode()
+    if dec is None:
+        return None
+    torch.set_num_threads(os.cpu_count())
+    key = (batch, L, dtype_name)
+    if key not in _REF_INPUTS:
+        _REF_INPUTS[key] = _reference_inputs(batch, L, dtype_name)
+    q, ks, vs, k_up, seg, u_by_q, inv_freq = _REF_INPUTS[key]
+    dec(q, ks, vs, k_up, seg, u_by_q, inv_freq, 128 ** -0.5)   # warm-up
+    times, t_all = [], time.perf_counter()
+    while len(times) < reps_min or (time.perf_counter() - t_all < seconds and len(times) < 50):
+        t0 = time.perf_counter()
+        dec(q, ks, vs, k_up, seg, u_by_q, inv_freq, 128 ** -0.5)
+        times.append(time.perf_counter() - t0)
+    ms = statistics.median(times) * 1e3
+    return batch / (ms * 1e-3), ms
+
+
+_REF_INPUTS = {}
+
+
+def _reference_inputs(batch, L, dtype_name):
+    import torch
+    from starkv_b200.workload import sample_ranks
+    dt = {"fp32": torch.float32, "bf16": torch.bfloat16}[dtype_name]
+    g = torch.Generator().manual_seed(0)
+    ranks, rv = sample_ranks(32, 0)
+    widths = [-(-r // 16) * 16 for r in ranks]
+    offsets = [sum(widths[:h]) for h in range(32)]
+    W = sum(widths)
+    k_up = torch.zeros(W, 128)
+    for r, o in zip(ranks, offsets):
+        k_up[o:o + r] = torch.randn(r, 128, generator=g) / r ** 0.5
+    key_states = torch.randn(batch, W, L, generator=g)
+    for r, o, w in zip(ranks, offsets, widths):
+        key_states[:, o + r:o + w] = 0
+    value_states = torch.randn(batch, L, rv, generator=g)
+    u_by_q = torch.randn(32, rv, 128, generator=g) / rv ** 0.5
+    q = torch.randn(batch, 32, 1, 128, generator=g)
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+    return (q.to(dt), key_states.to(dt), value_states.to(dt), k_up.to(dt), list(zip(offsets, ranks)), u_by_q.to(dt),
+            inv_freq)
+
+
+def cpu_baseline_line(seconds=10.0):
+    """cpu_baseline of the JSON line: the reference's own torch CPU math on a sample of
+    config 2 (4 of its 64 sequences, 8192 tokens, bf16 as the cache is), plus
+    BASELINE config 1 (batch 4, context 2048) in fp32 and bf16; the numpy oracle port
+    when the reference is not importable."""
+    main = reference_cpu_time(4, 8192, "bf16", seconds)
+    if main is None:
+        rate, desc = cpu_sample_time(False)
+        return {"value": round(rate, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": desc}
+    c1 = {dt: reference_cpu_time(4, 2048, dt, seconds=3.0, reps_min=5) for dt in ("fp32", "bf16")}
+    return {"value": round(main[0], 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+            "sample": "4 of config 2's sequences x 8192 tokens per call, bf16, the reference's own torch CPU "
+                      "decode (model.py _expand_ragged_k / _rope_tables / no-Triton branch) from baseline/_ref",
+            "ms_per_call": round(main[1], 2),
+            "config1_ms": {dt: (round(v[1], 2) if v else None) for dt, v in c1.items()},
+            "config1": "batch 4 x 2048 tokens, 32 heads, contiguous cache, median of >= 5 after 1 warm-up"}
+
+
 def cpu_sample_time(quant: bool, seconds: float = 12.0):
     """Reference algorithm (oracle port, numpy, all host cores) on whole sequences of
     the same workload; returns (sequences per second, sample description)."""
@@ -603,112 +738,161 @@ def ours(args):
             dist.barrier()
             dist.destroy_process_group()
         return
-    res = {}
-    cases = {"c2": (False,), "c3": (True,), "both": (False, True), "c4": (False, True)}[args.case]
-    for quant in cases:
-        layer, heads = build_layer(quant, world, rank, device, args.batch, args.context, args.parallel,
-                                   mixed=args.case == "c4")
-        cp = (rank, world) if dist_on and args.parallel == "context" else None
-        # sequence split (seqs): every rank decodes its own whole batch
-        ms, per_kernel, clocks, e2e_ms, h2d, d2h, last = measure(layer, device, args.steps, args.warmup, dist_on,
-                                                                 cp)
-        res[quant] = dict(layer=layer, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d,
-                          d2h=d2h, alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
-                          roof=roofline_for(layer, per_kernel, hbm_peak, cp))
-        if world == 1 and args.case in ("both", "c2", "c3") and not args.no_bar:
-            res[quant]["bar"] = triton_bar(layer, device, args.steps, sum(per_kernel), last)
-        del last
-        del layer
-        torch.cuda.empty_cache()
-    if rank == 0 and args.case == "c4":
-        # config 4 (mixed lengths, skewed ranks), both formats: one line, no baselines
-        line = {"case": "c4", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "parallelism": ("single" if world == 1 else f"dp{world} (sequences, a batch per GPU)"
-                                if args.parallel == "seqs" else f"cp{world} (context split)"
-                                if args.parallel == "context" else f"tp{world} (heads, LPT by rank)"),
-                "sequences": res[False]["layer"].n * (world if args.parallel == "seqs" else 1),
-                "tokens": int(sum(res[False]["layer"].seq_lens_host))}
-        reps = world if args.parallel == "seqs" else 1   # batches in the job (one per GPU under seqs)
-        for quant, key in ((False, "bf16"), (True, "q32")):
-            r = res[quant]
-            line[key] = {"ms_per_step": round(r["ms"], 4), "value": round(reps * r["layer"].n / (r["ms"] * 1e-3), 1),
-                         "unit": UNIT, "hbm_gbs": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
-                         "hbm_frac_step": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
-                         "k_width": r["layer"].k_width, "v_rank": r["layer"].v_rank,
-                         "kernel_ms": r["roof"]["kernel_ms"], "clocks": r["clocks"]}
-        print(json.dumps(line), flush=True)
-    elif rank == 0 and args.case != "both":
+    if args.case == "c4":
+        # config 4 alone (mixed lengths, skewed ranks), both formats: one line, no baselines
+        c4 = {key: decode_case(quant, True, args, world, rank, device, dist_on, hbm_peak)
+              for quant, key in ((False, "bf16"), (True, "q32"))}
+        if rank == 0:
+            print(json.dumps({"case": "c4", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                              **c4_summary(c4, args.parallel, world, hbm_peak)}), flush=True)
+    elif args.case in ("c2", "c3"):
         # single-configuration run (profiling): short line, no baselines
-        r = res[cases[0]]
-        print(json.dumps({"case": args.case, "batch": r["layer"].n, "context": r["layer"].seq_lens_host[0],
-                          "ms_per_step": round(r["ms"], 4), "kernel_ms": r["roof"]["kernel_ms"],
-                          "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
-                          "roofline_frac": r["roof"]["frac"], "gpu_bar": r.get("bar")}), flush=True)
-    elif rank == 0:
-        b = res[False]
-        n = b["layer"].n
-        reps = world if args.parallel == "seqs" else 1   # batches in the job (one per GPU under seqs)
-        cpu_rate, cpu_desc = (None, None)
-        if world == 1:
-            cpu_rate, cpu_desc = cpu_sample_time(False)
-        q = res[True]
-        line = {
-            "metric": METRIC, "value": round(reps * n / (b["ms"] * 1e-3), 1), "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(b["ms"], 4), "us_per_layer": round(b["ms"] * 1e3, 1),
-            "hbm_gbs": round(reps * b["alg"] / (b["ms"] * 1e-3) / 1e9, 1),
-            "hbm_frac_step": round(reps * b["alg"] / (b["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
-            "higher_is_better": True, "scaling": "strong" if world > 1 and args.parallel != "seqs" else "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config shapes)",
-            "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
-                                   "32 heads x 128, page 16, cache write + decode per step",
-                       "batch": 64, "global_batch": 64 * reps, "context": 8192,
-                       "heads_per_gpu": 32 if world == 1 or args.parallel != "heads" else 32 // world,
-                       "parallelism": ("single" if world == 1 else f"dp{world} (sequences: 64 per GPU, no collective)"
-                                       if args.parallel == "seqs" else f"cp{world} (context split, all heads per GPU)"
-                                       if args.parallel == "context" else f"tp{world} (heads)"),
-                       "l2": "inputs (2.9 GB cache) larger than L2; no flush"},
-            "roofline": dict(b["roof"], peak_kind=peak_kind),
-            "e2e": {"value": round(reps * n / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
-                    "h2d_bytes_per_step": b["h2d"], "d2h_bytes_per_step": b["d2h"],
-                    "ms_per_step": round(b["e2e_ms"], 4)},
-            "gpu_bar": {"bf16": b.get("bar"), "q32": q.get("bar")} if world == 1 and not args.no_bar else None,
-            "gpu_launches": (5 if world == 1 or args.parallel != "context" or rank == world - 1 else 4) * args.steps,
-            "clocks": b["clocks"],
-            "q32": {"workload": "config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
-                    "value": round(reps * q["layer"].n / (q["ms"] * 1e-3), 1), "unit": UNIT,
-                    "ms_per_step": round(q["ms"], 4), "us_per_layer": round(q["ms"] * 1e3, 1),
-                    "hbm_gbs": round(reps * q["alg"] / (q["ms"] * 1e-3) / 1e9, 1),
-                    "hbm_frac_step": round(reps * q["alg"] / (q["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
-                    "tflops": round(reps * q["flops"] / (q["ms"] * 1e-3) / 1e12, 1),
-                    "roofline": dict(q["roof"], peak_kind=peak_kind),
-                    "e2e_ms_per_step": round(q["e2e_ms"], 4), "clocks": q["clocks"]},
-        }
-        if cpu_rate is not None:
-            line["cpu_baseline"] = {"value": round(cpu_rate, 3), "unit": UNIT, "cores": os.cpu_count(),
-                                    "kind": "port", "sample": cpu_desc}
-        print(json.dumps(line), flush=True)
+        r = decode_case(args.case == "c3", False, args, world, rank, device, dist_on, hbm_peak,
+                        bar=world == 1 and "bar" not in args.skip)
+        if rank == 0:
+            print(json.dumps({"case": args.case, "batch": r["n"], "context": r["context"],
+                              "ms_per_step": round(r["ms"], 4), "kernel_ms": r["roof"]["kernel_ms"],
+                              "hbm_gbs": round(r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
+                              "roofline_frac": r["roof"]["frac"], "gpu_bar": r.get("bar")}), flush=True)
+    else:
+        bar = world == 1 and "bar" not in args.skip
+        b = decode_case(False, False, args, world, rank, device, dist_on, hbm_peak, bar=bar)
+        q = decode_case(True, False, args, world, rank, device, dist_on, hbm_peak, bar=bar)
+        heads = None
+        if dist_on and args.parallel != "heads" and "heads" not in args.skip:
+            heads = decode_case(False, False, args, world, rank, device, dist_on, hbm_peak, parallel="heads")
+        c4 = None
+        if "c4" not in args.skip:
+            c4 = {key: decode_case(quant, True, args, world, rank, device, dist_on, hbm_peak)
+                  for quant, key in ((False, "bf16"), (True, "q32"))}
+        model = None
+        if "model" not in args.skip:
+            model = model_measure(args, device, world, rank, dist_on, args.parallel)
+        if rank == 0:
+            reps = world if dist_on and args.parallel == "seqs" else 1   # batches in the job (seqs: one per GPU)
+            cpu_line = cpu_baseline_line() if world == 1 else None
+            par = ("single" if world == 1 else f"dp{world} (sequences: 64 per GPU, no collective)"
+                   if args.parallel == "seqs" else f"cp{world} (context split, all heads per GPU)"
+                   if args.parallel == "context" else f"tp{world} (heads, LPT by K width)")
+            cp_on = dist_on and args.parallel == "context"
+            line = {
+                "metric": METRIC, "value": round(reps * b["n"] / (b["ms"] * 1e-3), 1), "unit": UNIT,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(b["ms"], 4), "us_per_layer": round(b["ms"] * 1e3, 1),
+                "hbm_gbs": round(reps * b["alg"] / (b["ms"] * 1e-3) / 1e9, 1),
+                "hbm_frac_step": round(reps * b["alg"] / (b["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+                "higher_is_better": True, "scaling": "strong" if dist_on and args.parallel != "seqs" else "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config shapes)",
+                "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
+                                       "32 heads x 128, page 16, cache write + decode per step",
+                           "batch": 64, "global_batch": 64 * reps, "context": 8192,
+                           "heads_per_gpu": 32 if not dist_on or args.parallel != "heads" else 32 // world,
+                           "parallelism": par, "l2": "inputs (2.9 GB cache) larger than L2; no flush"},
+                "roofline": dict(b["roof"], peak_kind=peak_kind),
+                "e2e": {"value": round(reps * b["n"] / (b["e2e_ms"] * 1e-3), 1), "unit": UNIT,
+                        "h2d_bytes_per_step": b["h2d"], "d2h_bytes_per_step": b["d2h"],
+                        "ms_per_step": round(b["e2e_ms"], 4)},
+                "gpu_bar": {"bf16": b.get("bar"), "q32": q.get("bar")} if bar else None,
+                # our kernels per step on rank 0: fold, scores, P.V, lift, the cache write (the
+                # writing rank: all of them, or under the context split the last one), the combine
+                "gpu_launches": (4 + (0 if cp_on and world > 1 else 1) + (1 if cp_on else 0)) * args.steps,
+                "clocks": b["clocks"],
+                "q32": dict(step_summary(q, reps, world, hbm_peak, peak_kind),
+                            workload="config3: 3.2-bit paged decode, 64 seqs x 16384 tokens, pack + decode per step",
+                            tflops=round(reps * q["flops"] / (q["ms"] * 1e-3) / 1e12, 1)),
+            }
+            if heads is not None:
+                line["heads"] = dict(step_summary(heads, 1, world, hbm_peak, peak_kind),
+                                     workload="config2 with heads sharded tensor-parallel (LPT by K width); "
+                                              "the V latent is read whole on every rank", heads_per_gpu=32 // world)
+            if c4 is not None:
+                line["c4"] = c4_summary(c4, args.parallel, world, hbm_peak)
+            if model is not None:
+                line["model"] = model
+            if cpu_line is not None:
+                line["cpu_baseline"] = cpu_line
+            print(json.dumps(line), flush=True)
     if dist_on:
         dist.barrier()
         dist.destroy_process_group()
 
 
+def decode_case(quant, mixed, args, world, rank, device, dist_on, hbm_peak, bar=False, parallel=None):
+    """Build one configuration's layer (config 2 / 3, or config 4 when `mixed`),
+    time its step (`measure`) and, with `bar`, the reference's Triton decode on the
+    same inputs; returns the figures (the layer itself is freed)."""
+    import torch
+    parallel = parallel or args.parallel
+    batch, context = (None, None) if mixed else (args.batch, args.context)
+    layer, _ = build_layer(quant, world, rank, device, batch, context, parallel, mixed=mixed)
+    cp = (rank, world) if dist_on and parallel == "context" else None
+    ms, per_kernel, clocks, e2e_ms, h2d, d2h, last = measure(layer, device, args.steps, args.warmup, dist_on, cp)
+    r = dict(n=layer.n, context=layer.seq_lens_host[0], tokens=layer.kv_tokens(), k_width=layer.k_width,
+             v_rank=layer.v_rank, ms=ms, per_kernel=per_kernel, clocks=clocks, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h,
+             alg=layer.algorithmic_bytes(), flops=layer.algorithmic_flops(),
+             roof=roofline_for(layer, per_kernel, hbm_peak, cp))
+    if bar:
+        r["bar"] = triton_bar(layer, device, args.steps, sum(per_kernel), last)
+    del last, layer
+    torch.cuda.empty_cache()
+    return r
+
+
+def step_summary(r, reps, world, hbm_peak, peak_kind):
+    """Sub-object of the JSON line for one measured configuration."""
+    return {"value": round(reps * r["n"] / (r["ms"] * 1e-3), 1), "unit": UNIT,
+            "ms_per_step": round(r["ms"], 4), "us_per_layer": round(r["ms"] * 1e3, 1),
+            "hbm_gbs": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
+            "hbm_frac_step": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+            "roofline": dict(r["roof"], peak_kind=peak_kind), "e2e_ms_per_step": round(r["e2e_ms"], 4),
+            "clocks": r["clocks"]}
+
+
+def c4_summary(c4, parallel, world, hbm_peak):
+    """Config 4 (256 mixed-length sequences, skewed ranks), both formats."""
+    reps = world if world > 1 and parallel == "seqs" else 1
+    out = {"workload": "config4: 256 seqs, contexts seeded uniform in [1024, 32768], skewed ranks (K 16..128, "
+                       "V 32..128 per head), 32 heads, cache write / pack + decode per step",
+           "parallelism": ("single" if world == 1 else f"dp{world} (sequences, a batch per GPU)"
+                           if parallel == "seqs" else f"cp{world} (context split)"
+                           if parallel == "context" else f"tp{world} (heads, LPT by rank)"),
+           "sequences": c4["bf16"]["n"] * reps, "tokens": int(c4["bf16"]["tokens"])}
+    for key, r in c4.items():
+        out[key] = {"ms_per_step": round(r["ms"], 4), "value": round(reps * r["n"] / (r["ms"] * 1e-3), 1),
+                    "unit": UNIT, "hbm_gbs": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9, 1),
+                    "hbm_frac_step": round(reps * r["alg"] / (r["ms"] * 1e-3) / 1e9 / (hbm_peak * world), 4),
+                    "k_width": r["k_width"], "v_rank": r["v_rank"], "kernel_ms": r["roof"]["kernel_ms"],
+                    "clocks": r["clocks"]}
+    return out
+
+
 def reference(args):
+    """The reference arm: the reference's own torch CPU decode (reference_torch_decode)
+    on this host's cores, each step one call on 4 of config 2's sequences (bf16, 8192
+    tokens); the numpy oracle port when the reference is not importable. Rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    rates = []
+    import torch
+    dec = reference_torch_decode()
+    rates, desc, kind, dtype = [], None, "reference", "bf16"
     for i in range(args.warmup + args.steps):
-        r, desc = cpu_sample_time(False, seconds=2.0)
+        if dec is not None:
+            r = reference_cpu_time(4, 8192, "bf16", seconds=0.0, reps_min=1)[0]
+            desc = ("4 of config 2's sequences x 8192 tokens per step, bf16, the reference's own torch CPU decode "
+                    f"(model.py _expand_ragged_k / _rope_tables / no-Triton branch), {torch.get_num_threads()} threads")
+        else:
+            r, desc = cpu_sample_time(False, seconds=2.0)
+            kind, dtype = "port", "f32"
         if i >= args.warmup:
             rates.append(r)
     v = statistics.median(rates)
     line = {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "impl": "reference",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded, config shapes)",
+            "higher_is_better": True, "dtype": dtype, "data": "synthetic (seeded, config shapes)",
             "config": {"workload": "config2: paged bf16 low-rank decode, 1 layer, 64 seqs x 8192 tokens, "
-                                   "32 heads x 128 (CPU: reference algorithm, whole sequences per sample)"},
-            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                                   "32 heads x 128 (CPU: a bounded sample of the sequences per step)"},
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": kind,
                              "sample": desc},
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -722,14 +906,20 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4", "layer", "model"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
-    ap.add_argument("--parallel", default="seqs", choices=["seqs", "context", "heads"],
-                    help="N > 1: a batch of sequences per GPU (weak scaling, default); or one batch split over "
-                         "the GPUs by each sequence's tiles (context) or by heads")
+    ap.add_argument("--parallel", default="context", choices=["seqs", "context", "heads"],
+                    help="N > 1: one batch split over the GPUs by each sequence's tiles (context, default; the "
+                         "head split is measured beside it), or by heads; or a batch of sequences per GPU (seqs, "
+                         "weak scaling)")
+    ap.add_argument("--skip", default="", help="comma list of parts of the default run to leave out: "
+                                               "heads, c4, model, bar")
+    ap.add_argument("--model-weights", default="checkpoint", choices=["checkpoint", "random"],
+                    help="config 5: K/V factors from a synthetic fused_weights.pt (default) or drawn in place")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling small cases)")
     ap.add_argument("--context", type=int, default=None, help="override the context (profiling small cases)")
     ap.add_argument("--no-bar", action="store_true", help="skip timing the reference's Triton kernels")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
+    a.skip = {x for x in a.skip.split(",") if x} | ({"bar"} if a.no_bar else set())
     if a.impl == "reference":
         reference(a)
     else:

@@ -1,7 +1,8 @@
 // Small kernels around the two tensor-core passes:
 //   fold_kernel   AB = fold(q, U) * scale (paged_quant.py:223-255), the f16 copy of
 //                 the rotary table rows, and per-call accumulator init;
-//   lift_kernel   out[b,h,:] = pv[b,h,:] / l[b,h] . v_up_by_q[h] (paged_decode.py:222-226);
+//   lift_kernel   out[b,h,:] = pv[b,h,:] / l[b,h] . v_up_by_q[h] (paged_decode.py:222-226), for
+//                 layouts the cluster lift (lift.cu) does not take (f32 or strided v_up);
 //   pack_k/v      3.2-bit write side (paged_quant.py:139-216), bit-exact with
 //                 kv_quant._q (kv_quant.py:111-121): IEEE division, round half even;
 //   cache_write   bf16 cache write (attention.py:179-185).
@@ -14,7 +15,8 @@ namespace starkv {
 // fold + rotary table + init (one launch)
 // ---------------------------------------------------------------------------
 
-constexpr int kFoldLanes = 16;   // K lanes per 128-thread block (8 threads x 8 values each)
+constexpr int kFoldLanes = 64;   // K lanes per 128-thread block
+constexpr int kFoldRows = 16;    // lanes one pass of the block covers (8 threads x 8 values each)
 
 // 8 consecutive elements (stride `st`) as floats: one or two 16-byte loads when the
 // run is contiguous and aligned, scalar loads otherwise.
@@ -40,7 +42,8 @@ template <class TQ, class TU>
 __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fold_blocks, int n_cs_blocks) {
   const int bid = blockIdx.x;
   if (bid < n_fold_blocks) {
-    // block -> (b, j, 16 lanes); thread -> (lane, 8 consecutive i of 0..63)
+    // block -> (b, j, 64 lanes); thread -> 8 consecutive i of 0..63 of lanes
+    // lr, lr + 16, lr + 32, lr + 48 (four independent rows: their loads overlap)
     __shared__ int head_of[kFoldLanes];
     const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
     const int bj = bid / lanes_per_seq;
@@ -68,43 +71,47 @@ __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fol
       head_of[threadIdx.x] = head;
     }
     __syncthreads();
-    const int lr = threadIdx.x >> 3, i0 = (threadIdx.x & 7) * 8;
-    const int r = r0 + lr;
-    if (r >= p.k_width) return;
     const int b = bj / p.group, j = bj % p.group;
-    const int head = head_of[lr];
-    __half av[8], bv[8];
-    if (head < 0) {
+    const int i0 = (threadIdx.x & 7) * 8;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) av[k] = bv[k] = __float2half_rn(0.f);
-    } else {
-      const int hq = head * p.group + j;
-      const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)hq * p.q_s1;
-      const TU* up = reinterpret_cast<const TU*>(p.k_up) + (int64_t)r * p.ku_s0;
-      float q0[8], q1[8], u0[8], u1[8];
-      load8(qp + (int64_t)i0 * p.q_s2, p.q_s2, q0);
-      load8(qp + (int64_t)(i0 + 64) * p.q_s2, p.q_s2, q1);
-      load8(up + (int64_t)i0 * p.ku_s1, p.ku_s1, u0);
-      load8(up + (int64_t)(i0 + 64) * p.ku_s1, p.ku_s1, u1);
+    for (int pass = 0; pass < kFoldLanes / kFoldRows; ++pass) {
+      const int lr = pass * kFoldRows + (threadIdx.x >> 3);
+      const int r = r0 + lr;
+      if (r >= p.k_width) break;
+      const int head = head_of[lr];
+      __align__(16) __half av[8], bv[8];
+      if (head < 0) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float a0 = q0[k], a1 = q1[k], w0 = u0[k], w1 = u1[k];
-        av[k] = __float2half_rn((a0 * w0 + a1 * w1) * p.scale);
-        bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
+        for (int k = 0; k < 8; ++k) av[k] = bv[k] = __float2half_rn(0.f);
+      } else {
+        const int hq = head * p.group + j;
+        const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)hq * p.q_s1;
+        const TU* up = reinterpret_cast<const TU*>(p.k_up) + (int64_t)r * p.ku_s0;
+        float q0[8], q1[8], u0[8], u1[8];
+        load8(qp + (int64_t)i0 * p.q_s2, p.q_s2, q0);
+        load8(qp + (int64_t)(i0 + 64) * p.q_s2, p.q_s2, q1);
+        load8(up + (int64_t)i0 * p.ku_s1, p.ku_s1, u0);
+        load8(up + (int64_t)(i0 + 64) * p.ku_s1, p.ku_s1, u1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float a0 = q0[k], a1 = q1[k], w0 = u0[k], w1 = u1[k];
+          av[k] = __float2half_rn((a0 * w0 + a1 * w1) * p.scale);
+          bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
+        }
       }
-    }
-    if (p.ab_image) {
-      // the 128-byte-swizzled K-major tile the score MMA reads as its B operand
-      const int nc = (p.k_width + 127) / 128;
-      const int c = r >> 7, half = (r >> 6) & 1, i = r & 63;
-      __half* blk = p.ab + ((((int64_t)bj * nc + c) * 2 + half) << 13);   // 8192 halves per block
-      const int unit = (threadIdx.x & 7) ^ (i & 7);
-      *reinterpret_cast<uint4*>(blk + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(av);
-      *reinterpret_cast<uint4*>(blk + 4096 + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(bv);
-    } else {
-      __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
-      *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
-      *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
+      if (p.ab_image) {
+        // the 128-byte-swizzled K-major tile the score MMA reads as its B operand
+        const int nc = (p.k_width + 127) / 128;
+        const int c = r >> 7, half = (r >> 6) & 1, i = r & 63;
+        __half* blk = p.ab + ((((int64_t)bj * nc + c) * 2 + half) << 13);   // 8192 halves per block
+        const int unit = (threadIdx.x & 7) ^ (i & 7);
+        *reinterpret_cast<uint4*>(blk + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(av);
+        *reinterpret_cast<uint4*>(blk + 4096 + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(bv);
+      } else {
+        __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
+        *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
+        *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
+      }
     }
     return;
   }
@@ -149,7 +156,9 @@ int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream) {
   const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
   const int n_fold = p.n * p.group * lanes_per_seq;
   const int n_cs = (int)(((int64_t)p.l_pad * 16 + 127) / 128);   // one thread per 16-byte unit
-  const int n_init = 296;
+  // the accumulator clear: up to 8 blocks per SM of float4 stores in a grid-stride loop
+  const int64_t init_work = p.m_count + (p.pv_count >> 2);
+  const int n_init = (int)(init_work < 1184 * 128 ? (init_work + 127) / 128 + 1 : 1184);
   with_float_type(p.q_dtype, [&](auto tq) {
     with_float_type(p.k_up_dtype, [&](auto tu) {
       fold_kernel<decltype(tq), decltype(tu)><<<n_fold + n_cs + n_init, 128, 0, stream>>>(p, n_fold, n_cs);
@@ -358,6 +367,8 @@ __global__ void __launch_bounds__(kLiftGT * kLiftGroups) lift_kernel(const LiftP
 }
 
 int launch_lift(const LiftParams& p, cudaStream_t stream) {
+  const int fast = launch_lift_cluster(p, stream);   // the common layout (lift.cu)
+  if (fast >= 0) return fast;
   dim3 grid(p.num_heads, (p.head_dim + 31) / 32, (p.n + kLiftBT - 1) / kLiftBT);
   // 16-byte v_up loads: 2-byte elements, unit stride along d, every run of 8 aligned
   const int es = p.v_up_dtype == STARKV_F32 ? 4 : 2;

@@ -123,5 +123,6 @@ int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab
                   cudaStream_t stream);
 int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms, cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
+int launch_lift_cluster(const LiftParams& p, cudaStream_t stream);   // -1: layout not taken
 
 }  // namespace starkv
