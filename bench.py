@@ -8,7 +8,9 @@ attention (bf16 codes: configuration 2 of BASELINE.json, 64 sequences x 8192
 tokens). The 3.2-bit configuration 3 (64 x 16384) is measured the same way and
 reported under "q32". Inputs are seeded synthetic tensors with the configs'
 shapes and distributions (starkv_b200.workload); every step reads a >2 GB cache,
-far larger than the 126 MB L2, so no flush is needed between steps.
+far larger than the 126 MB L2, so no flush is needed between steps. Each step is
+captured once in a CUDA graph and replayed, as a serving engine runs the decode
+(the line's clocks.mode says so; eager when capture is not possible).
 
 Every default run also measures, in the same line: config 4 (256 mixed-length
 sequences, skewed ranks, both formats: "c4"), config 5 (the whole 32-layer model's
@@ -217,6 +219,27 @@ def measure(layer, device, steps, warmup, dist_on, cp=None):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    graphs = []   # released before returning (they may hold NCCL calls)
+
+    def graphed(fn):
+        """fn captured in a CUDA graph (the decode path allocates and synchronises
+        nothing, so it captures as a serving engine runs it); eager if capture fails."""
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            torch.cuda.synchronize()
+            graphs.append(g)
+            return g.replay, "cuda graph"
+        except Exception as e:   # noqa: BLE001 - recorded in the line, timed eagerly
+            torch.cuda.synchronize()
+            return fn, f"eager (capture failed: {type(e).__name__})"
 
     def timed(fn, k):
         if dist_on:
@@ -236,9 +259,13 @@ def measure(layer, device, steps, warmup, dist_on, cp=None):
             dist.barrier()
         return ms
 
+    run, mode = graphed(step)
+    for _ in range(2):
+        run()
     clk = Clocks(device)
-    ms = timed(step, steps)
+    ms = timed(run, steps)
     clocks = clk.stop()
+    clocks["mode"] = mode
 
     # per-kernel durations, live CUDA events on the launching stream (separate pass)
     lib = _lib.lib()
@@ -271,11 +298,15 @@ def measure(layer, device, steps, warmup, dist_on, cp=None):
         hout.copy_(o, non_blocking=True)
     for _ in range(2):
         e2e_step()
-    e2e_ms = timed(e2e_step, steps)
+    e2e_run, _ = graphed(e2e_step)
+    for _ in range(2):
+        e2e_run()
+    e2e_ms = timed(e2e_run, steps)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hbt, hsl))
     d2h = hout.numel() * hout.element_size()
     last = step()
     torch.cuda.synchronize()
+    graphs.clear()
     return ms, per_kernel, clocks, e2e_ms, h2d, d2h, last
 
 

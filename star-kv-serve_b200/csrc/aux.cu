@@ -15,8 +15,11 @@ namespace starkv {
 // fold + rotary table + init (one launch)
 // ---------------------------------------------------------------------------
 
-constexpr int kFoldLanes = 64;   // K lanes per 128-thread block
+constexpr int kFoldLanes = 64;   // K lanes per fold block
 constexpr int kFoldRows = 16;    // lanes one pass of the block covers (8 threads x 8 values each)
+constexpr int kFoldSeqs = 4;     // (sequence, query head of the group) pairs per fold block
+constexpr int kFoldQHeads = 8;   // query rows staged per pair (the heads of 64 lanes)
+constexpr int kFoldUPitch = 128 + 8;   // staged k_up row (elements): 16-byte aligned, banks spread
 
 // 8 consecutive elements (stride `st`) as floats: one or two 16-byte loads when the
 // run is contiguous and aligned, scalar loads otherwise.
@@ -42,12 +45,18 @@ template <class TQ, class TU>
 __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fold_blocks, int n_cs_blocks) {
   const int bid = blockIdx.x;
   if (bid < n_fold_blocks) {
-    // block -> (b, j, 64 lanes); thread -> 8 consecutive i of 0..63 of lanes
-    // lr, lr + 16, lr + 32, lr + 48 (four independent rows: their loads overlap)
+    // block -> (64 lanes, kFoldSeqs (b, j) pairs). The lanes' k_up rows are staged
+    // once and serve every pair; each pair's query rows of the lanes' heads are
+    // staged too, so global memory sees each input about once. thread -> 8
+    // consecutive i of 0..63 of lanes lr, lr + 16, lr + 32, lr + 48.
     __shared__ int head_of[kFoldLanes];
-    const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
-    const int bj = bid / lanes_per_seq;
-    const int r0 = (bid % lanes_per_seq) * kFoldLanes;
+    __shared__ int hmin_s;
+    __shared__ __align__(16) TU u_s[kFoldLanes][kFoldUPitch];
+    __shared__ __align__(16) float q_s[kFoldQHeads][128];
+    const int lane_tiles = (p.k_width + kFoldLanes - 1) / kFoldLanes;
+    const int r0 = (bid % lane_tiles) * kFoldLanes;
+    const int bj0 = (bid / lane_tiles) * kFoldSeqs;
+    const int bj1 = min(bj0 + kFoldSeqs, p.n * p.group);
     if (threadIdx.x < kFoldLanes) {
       const int r = r0 + threadIdx.x;
       int head = -1;
@@ -70,48 +79,96 @@ __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fol
       }
       head_of[threadIdx.x] = head;
     }
-    __syncthreads();
-    const int b = bj / p.group, j = bj % p.group;
-    const int i0 = (threadIdx.x & 7) * 8;
+    {
+      // k_up rows of the 64 lanes (zero past k_width): thread -> (row, half of 64 values)
+      const int row = threadIdx.x >> 1, c0 = (threadIdx.x & 1) * 64;
+      const int r = r0 + row;
+      const TU* up = reinterpret_cast<const TU*>(p.k_up) + (int64_t)r * p.ku_s0 + (int64_t)c0 * p.ku_s1;
+      const bool vec = p.ku_s1 == 1 && (reinterpret_cast<uintptr_t>(up) & 15) == 0;
 #pragma unroll
-    for (int pass = 0; pass < kFoldLanes / kFoldRows; ++pass) {
-      const int lr = pass * kFoldRows + (threadIdx.x >> 3);
-      const int r = r0 + lr;
-      if (r >= p.k_width) break;
-      const int head = head_of[lr];
-      __align__(16) __half av[8], bv[8];
-      if (head < 0) {
+      for (int k = 0; k < 64; k += 16 / (int)sizeof(TU)) {
+        constexpr int kPer = 16 / (int)sizeof(TU);
+        if (r < p.k_width && vec) {
+          *reinterpret_cast<uint4*>(&u_s[row][c0 + k]) = *reinterpret_cast<const uint4*>(up + k);
+        } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) av[k] = bv[k] = __float2half_rn(0.f);
-      } else {
-        const int hq = head * p.group + j;
-        const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)hq * p.q_s1;
-        const TU* up = reinterpret_cast<const TU*>(p.k_up) + (int64_t)r * p.ku_s0;
-        float q0[8], q1[8], u0[8], u1[8];
-        load8(qp + (int64_t)i0 * p.q_s2, p.q_s2, q0);
-        load8(qp + (int64_t)(i0 + 64) * p.q_s2, p.q_s2, q1);
-        load8(up + (int64_t)i0 * p.ku_s1, p.ku_s1, u0);
-        load8(up + (int64_t)(i0 + 64) * p.ku_s1, p.ku_s1, u1);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float a0 = q0[k], a1 = q1[k], w0 = u0[k], w1 = u1[k];
-          av[k] = __float2half_rn((a0 * w0 + a1 * w1) * p.scale);
-          bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
+          for (int e = 0; e < kPer; ++e) u_s[row][c0 + k + e] = r < p.k_width ? up[(int64_t)(k + e) * p.ku_s1] : TU{};
         }
       }
-      if (p.ab_image) {
-        // the 128-byte-swizzled K-major tile the score MMA reads as its B operand
-        const int nc = (p.k_width + 127) / 128;
-        const int c = r >> 7, half = (r >> 6) & 1, i = r & 63;
-        __half* blk = p.ab + ((((int64_t)bj * nc + c) * 2 + half) << 13);   // 8192 halves per block
-        const int unit = (threadIdx.x & 7) ^ (i & 7);
-        *reinterpret_cast<uint4*>(blk + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(av);
-        *reinterpret_cast<uint4*>(blk + 4096 + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(bv);
-      } else {
-        __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
-        *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
-        *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int m = p.num_kv_heads;
+      for (int i = 0; i < kFoldLanes; ++i)
+        if (head_of[i] >= 0) m = min(m, head_of[i]);
+      hmin_s = m;
+    }
+    __syncthreads();
+    const int hmin = hmin_s;
+    const int i0 = (threadIdx.x & 7) * 8;
+    for (int bj = bj0; bj < bj1; ++bj) {
+      const int b = bj / p.group, j = bj % p.group;
+      // query rows of heads hmin .. hmin + 7 (the lanes' heads, lanes being in head order)
+      for (int e = threadIdx.x; e < kFoldQHeads * 16; e += blockDim.x) {
+        const int hh = e >> 4, c = (e & 15) * 8;
+        const int h = hmin + hh;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (h < p.num_kv_heads) {
+          const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)(h * p.group + j) * p.q_s1;
+          load8(qp + (int64_t)c * p.q_s2, p.q_s2, v);
+        }
+        *reinterpret_cast<float4*>(&q_s[hh][c]) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(&q_s[hh][c + 4]) = make_float4(v[4], v[5], v[6], v[7]);
       }
+      __syncthreads();
+#pragma unroll
+      for (int pass = 0; pass < kFoldLanes / kFoldRows; ++pass) {
+        const int lr = pass * kFoldRows + (threadIdx.x >> 3);
+        const int r = r0 + lr;
+        if (r >= p.k_width) break;
+        const int head = head_of[lr];
+        __align__(16) __half av[8], bv[8];
+        if (head < 0) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) av[k] = bv[k] = __float2half_rn(0.f);
+        } else {
+          float q0[8], q1[8], u0[8], u1[8];
+          if (head - hmin < kFoldQHeads) {
+            const float* qr = q_s[head - hmin];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              q0[k] = qr[i0 + k];
+              q1[k] = qr[i0 + 64 + k];
+            }
+          } else {   // lanes of more than 8 heads in one block (not from k_tables): read directly
+            const TQ* qp = reinterpret_cast<const TQ*>(p.q) + (int64_t)b * p.q_s0 + (int64_t)(head * p.group + j) * p.q_s1;
+            load8(qp + (int64_t)i0 * p.q_s2, p.q_s2, q0);
+            load8(qp + (int64_t)(i0 + 64) * p.q_s2, p.q_s2, q1);
+          }
+          load8(&u_s[lr][i0], 1, u0);
+          load8(&u_s[lr][i0 + 64], 1, u1);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float a0 = q0[k], a1 = q1[k], w0 = u0[k], w1 = u1[k];
+            av[k] = __float2half_rn((a0 * w0 + a1 * w1) * p.scale);
+            bv[k] = __float2half_rn((a1 * w0 - a0 * w1) * p.scale);
+          }
+        }
+        if (p.ab_image) {
+          // the 128-byte-swizzled K-major tile the score MMA reads as its B operand
+          const int nc = (p.k_width + 127) / 128;
+          const int c = r >> 7, half = (r >> 6) & 1, i = r & 63;
+          __half* blk = p.ab + ((((int64_t)bj * nc + c) * 2 + half) << 13);   // 8192 halves per block
+          const int unit = (threadIdx.x & 7) ^ (i & 7);
+          *reinterpret_cast<uint4*>(blk + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(av);
+          *reinterpret_cast<uint4*>(blk + 4096 + i * 64 + unit * 8) = *reinterpret_cast<const uint4*>(bv);
+        } else {
+          __half* dst = p.ab + ((int64_t)bj * p.k_width + r) * 128;
+          *reinterpret_cast<uint4*>(dst + i0) = *reinterpret_cast<const uint4*>(av);
+          *reinterpret_cast<uint4*>(dst + 64 + i0) = *reinterpret_cast<const uint4*>(bv);
+        }
+      }
+      __syncthreads();   // q_s is rewritten for the next pair
     }
     return;
   }
@@ -153,8 +210,8 @@ __global__ void __launch_bounds__(128) fold_kernel(const FoldParams p, int n_fol
 
 int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream) {
   (void)quant;
-  const int lanes_per_seq = (p.k_width + kFoldLanes - 1) / kFoldLanes;
-  const int n_fold = p.n * p.group * lanes_per_seq;
+  const int lane_tiles = (p.k_width + kFoldLanes - 1) / kFoldLanes;
+  const int n_fold = lane_tiles * ((p.n * p.group + kFoldSeqs - 1) / kFoldSeqs);
   const int n_cs = (int)(((int64_t)p.l_pad * 16 + 127) / 128);   // one thread per 16-byte unit
   // the accumulator clear: up to 8 blocks per SM of float4 stores in a grid-stride loop
   const int64_t init_work = p.m_count + (p.pv_count >> 2);
