@@ -41,7 +41,10 @@
 //               from HBM) gathered through the block table;
 //   warp 1      TMEM owner (pair allocation, all 512 columns); in CTA 0 also the MMA issuer;
 //   warps 2-17  epilogue: thread = token row (TMEM lane) x 32-lane group of the
-//               chunk; per-head partial sums are merged with shared-memory atomics.
+//               chunk. Each 16-lane tile's partial logit goes to its own f16 slot
+//               (one writer per tile and token); the tile pass adds a head's tiles.
+//               Layers too wide for those slots merge per-head sums with
+//               shared-memory atomics instead.
 #include "starkv_common.cuh"
 #include "starkv_kernels.h"
 
@@ -83,11 +86,13 @@ struct SharedCtl {
 
 // Shared memory carve-up (byte offsets from the 1024-aligned base).
 struct SmemLayout {
-  int cs, ab, codes, code_slot, sc, logits, tiles, prefix, sbeg, ctl, total;
+  int cs, ab, codes, code_slot, sc, logits, tiles, hspan, prefix, sbeg, ctl, total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int k_width, int code_pitch,
-                                                  int sc_pitch) {
+// parts: the epilogue stores one f16 partial per (16-lane tile, token) [NC * 8][128]
+// instead of adding per-head f32 sums [H][129] with shared-memory atomics.
+__host__ __device__ inline SmemLayout smem_layout(bool quant, bool parts, int H, int n, int k_width,
+                                                  int code_pitch, int sc_pitch) {
   SmemLayout L;
   const int ab_slots = quant ? Cfg<true>::kAbSlots : Cfg<false>::kAbSlots;
   const int nc = (k_width + kChunk - 1) / kChunk;
@@ -97,8 +102,9 @@ __host__ __device__ inline SmemLayout smem_layout(bool quant, int H, int n, int 
   L.code_slot = (kTile * code_pitch + 127) & ~127;
   L.sc = L.codes + kCodeSlots * L.code_slot;
   L.logits = L.sc + (quant ? (kTile * sc_pitch + 127) & ~127 : 0);
-  L.tiles = (L.logits + H * (kTile + 1) * 4 + 15) & ~15;
-  L.prefix = L.tiles + nc * (kChunk / 16) * 4;
+  L.tiles = (L.logits + (parts ? nc * (kChunk / 16) * kTile * 2 : H * (kTile + 1) * 4) + 15) & ~15;
+  L.hspan = L.tiles + nc * (kChunk / 16) * 4;   // [H] first tile | tile count << 16
+  L.prefix = L.hspan + H * 4;
   L.sbeg = L.prefix + (n + 1) * 4;
   L.ctl = (L.sbeg + n * 4 + 15) & ~15;
   L.total = L.ctl + (int)sizeof(SharedCtl);
@@ -126,11 +132,12 @@ int code_pitch_bytes(int bytes) {
 
 int scores_window_bytes(bool quant) { return quant ? Cfg<true>::kWinBytes : Cfg<false>::kWinBytes; }
 
-size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch) {
-  return (size_t)smem_layout(quant, num_kv_heads, n, k_width, code_pitch, sc_pitch).total + 1024;
+size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch,
+                         bool parts) {
+  return (size_t)smem_layout(quant, parts, num_kv_heads, n, k_width, code_pitch, sc_pitch).total + 1024;
 }
 
-template <bool QUANT, bool F16>
+template <bool QUANT, bool F16, bool PARTS>
 __global__ void __launch_bounds__(kThreads, 1)
 scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__ CUtensorMap tm_ab,
               const __grid_constant__ CUtensorMap tm_code, const __grid_constant__ CUtensorMap tm_tail,
@@ -142,9 +149,11 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
   const int H = p.num_kv_heads;
   const int NT = p.k_width / 16;
   const int NC = (p.k_width + kChunk - 1) / kChunk;
-  const SmemLayout SL = smem_layout(QUANT, H, p.n, p.k_width, p.code_pitch, p.sc_pitch);
-  float* logits = reinterpret_cast<float*>(smem + SL.logits);    // [H][129]
+  const SmemLayout SL = smem_layout(QUANT, PARTS, H, p.n, p.k_width, p.code_pitch, p.sc_pitch);
+  float* logits = reinterpret_cast<float*>(smem + SL.logits);    // !PARTS: [H][129] per-head sums
+  __half* parts = reinterpret_cast<__half*>(smem + SL.logits);   // PARTS: [NC * 8][128] per-tile partials
   int* tiles = reinterpret_cast<int*>(smem + SL.tiles);           // [NC * 8], -1 past NT
+  int* hspan = reinterpret_cast<int*>(smem + SL.hspan);           // [H] first tile | count << 16
   int* prefix = reinterpret_cast<int*>(smem + SL.prefix);         // [n+1] item prefix over sequences
   int* sbeg = reinterpret_cast<int*>(smem + SL.sbeg);             // [n] first 256-token tile of this rank
   SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem + SL.ctl);
@@ -186,7 +195,25 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
     }
     tiles[t] = entry;
   }
-  for (int i = threadIdx.x; i < H * (kTile + 1); i += blockDim.x) logits[i] = 0.f;
+  if (!PARTS)
+    for (int i = threadIdx.x; i < H * (kTile + 1); i += blockDim.x) logits[i] = 0.f;
+  // each head's range of 16-lane tiles, first | span << 16 (the tile pass adds the
+  // partials of the range's tiles that belong to the head)
+  if (PARTS)
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
+      int first = 0, span = 0;
+      if (QUANT) {
+        for (int t = 0; t < NT; ++t)
+          if (p.tile_head[t] == h) {
+            if (span == 0) first = t;
+            span = t - first + 1;
+          }
+      } else {
+        first = min(max(p.k_head_offsets[h], 0), NT * 16) / 16;
+        span = min((max(p.k_ranks[h], 0) + 15) / 16 + 1, NT - first);
+      }
+      hspan[h] = first | (span << 16);
+    }
   if (threadIdx.x == 0) {
     // In CTA 0, ab_full / cs_full count the TMA bytes of BOTH CTAs and tempty the
     // epilogue warps of both; the peer's own copies of those barriers stay unused.
@@ -390,6 +417,8 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       for (int i = 0; i < 4; ++i) ai[i] = make_float2(0.f, 0.f);
       ao[0] = ao[1] = make_float2(0.f, 0.f);
       int cur_h = -1;
+      int sc_h = -1;            // PARTS, 3.2-bit: head whose scales so_c / si_c hold
+      float so_c = 0.f, si_c = 0.f;
       auto flush = [&]() {
         const float all = ((ai[0].x + ai[0].y) + (ai[1].x + ai[1].y)) + ((ai[2].x + ai[2].y) + (ai[3].x + ai[3].y));
         float v;
@@ -452,7 +481,11 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
             const int meta = hh == 0 ? m2.x : m2.y;
             if (meta < 0) continue;
             const int h = meta & 0xFFFF;
-            if (h != cur_h) {
+            if (PARTS) {   // the sums below are this tile's alone
+#pragma unroll
+              for (int i = 0; i < 4; ++i) ai[i] = make_float2(0.f, 0.f);
+              ao[0] = ao[1] = make_float2(0.f, 0.f);
+            } else if (h != cur_h) {
               if (cur_h >= 0) flush();
               cur_h = h;
             }
@@ -500,6 +533,24 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
                 }
               }
             }
+            if (PARTS) {
+              // this tile's partial logit (scales of its head applied) -> its own slot:
+              // one writer per (tile, token), no atomics
+              const float2 s01 = __fadd2_rn(__fadd2_rn(ai[0], ai[1]), __fadd2_rn(ai[2], ai[3]));
+              float v = s01.x + s01.y;
+              if (QUANT) {
+                if (h != sc_h) {
+                  const uint32_t sw = *reinterpret_cast<const uint32_t*>(smem + SL.sc + row * p.sc_pitch + p.ks_off +
+                                                                         4 * h - p.sc_x0);
+                  so_c = __uint_as_float(sw << 16);
+                  si_c = __uint_as_float(sw & 0xFFFF0000u);
+                  sc_h = h;
+                }
+                const float out = (ao[0].x + ao[0].y) + (ao[1].x + ao[1].y);
+                v = si_c * v + (so_c - si_c) * out;
+              }
+              parts[(c * kGroups * 2 + 2 * g + hh) * kTile + row] = __float2half_rn(v);
+            }
           }
         }
         tc_fence_before();
@@ -510,7 +561,7 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
         }
         if (cw == C::kChunksPerWin - 1 || c == NC - 1) ++code_it;
       }
-      if (cur_h >= 0) flush();
+      if (!PARTS && cur_h >= 0) flush();
       if (QUANT) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->sc_empty);
@@ -520,16 +571,30 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
       // next tile's atomic flushes: warp ew owns heads ew, ew + 16, ...; lane l tokens
       // l, l + 32, l + 64, l + 96 (consecutive words: conflict-free) ----
       for (int h = ew; h < H; h += kEpiWarps) {
-        float* lrow = logits + h * (kTile + 1);
         float v[4];
         float m = -INFINITY;
+        if (PARTS) {
+          // the head's logit is the sum of its tiles' partials
+          const int sp = hspan[h], tf = sp & 0xFFFF, cnt = sp >> 16;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int t = lane + 32 * i;
-          v[i] = lrow[t];
-          lrow[t] = 0.f;
-          if (t0 + t < L) m = fmaxf(m, v[i]);
+          for (int i = 0; i < 4; ++i) v[i] = 0.f;
+          for (int k = 0; k < cnt; ++k) {
+            if ((tiles[tf + k] & 0xFFFF) != h) continue;   // -1 (past the lanes) or another head
+            const __half* pr = parts + (tf + k) * kTile;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] += __half2float(pr[lane + 32 * i]);
+          }
+        } else {
+          float* lrow = logits + h * (kTile + 1);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            v[i] = lrow[lane + 32 * i];
+            lrow[lane + 32 * i] = 0.f;
+          }
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (t0 + lane + 32 * i < L) m = fmaxf(m, v[i]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (t0 < L) {
@@ -562,11 +627,11 @@ scores_kernel(const __grid_constant__ CUtensorMap tm_cs, const __grid_constant__
 
 namespace {
 
-template <bool QUANT, bool F16>
+template <bool QUANT, bool F16, bool PARTS>
 int launch_pairs(const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
                  const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
                  size_t smem, cudaStream_t stream) {
-  auto fn = scores_kernel<QUANT, F16>;
+  auto fn = scores_kernel<QUANT, F16, PARTS>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return STARKV_ECUDA;
   cudaLaunchConfig_t cfg = {};
@@ -584,8 +649,8 @@ int launch_pairs(const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUten
   // paired inside a GPC stay idle rather than run a second wave)
   int dev = 0;
   cudaGetDevice(&dev);
-  static int max_pairs[64][2] = {};
-  int& mp = max_pairs[dev & 63][QUANT ? 1 : 0];
+  static int max_pairs[64][2][2] = {};
+  int& mp = max_pairs[dev & 63][QUANT ? 1 : 0][PARTS ? 1 : 0];
   if (mp == 0) {
     cfg.gridDim = dim3(num_sms & ~1);
     int clusters = 0;
@@ -603,12 +668,21 @@ int launch_pairs(const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUten
 int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
                   const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
                   cudaStream_t stream) {
-  const size_t smem = scores_smem_bytes(quant, p.num_kv_heads, p.n, p.k_width, p.code_pitch, p.sc_pitch);
+  // per-tile partials when their shared memory fits (wide layers fall back to the
+  // per-head sums merged with shared-memory atomics)
+  const size_t smem_p = scores_smem_bytes(quant, p.num_kv_heads, p.n, p.k_width, p.code_pitch, p.sc_pitch, true);
+  const size_t smem_a = scores_smem_bytes(quant, p.num_kv_heads, p.n, p.k_width, p.code_pitch, p.sc_pitch, false);
+  const bool parts = smem_p <= 227 * 1024;
+  const size_t smem = parts ? smem_p : smem_a;
   if (smem > 227 * 1024) return STARKV_EINVAL;
-  if (quant) return launch_pairs<true, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
+  if (quant)
+    return parts ? launch_pairs<true, false, true>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream)
+                 : launch_pairs<true, false, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
   if (p.cache_dtype == STARKV_F16)
-    return launch_pairs<false, true>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
-  return launch_pairs<false, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
+    return parts ? launch_pairs<false, true, true>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream)
+                 : launch_pairs<false, true, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
+  return parts ? launch_pairs<false, false, true>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream)
+               : launch_pairs<false, false, false>(tm_cs, tm_ab, tm_code, tm_tail, tm_sc, p, num_sms, smem, stream);
 }
 
 }  // namespace starkv

@@ -107,7 +107,8 @@ struct FoldParams {
   int32_t* status;
 };
 
-size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch);
+size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch,
+                         bool parts);
 int code_pitch_bytes(int bytes);
 int scores_window_bytes(bool quant);
 size_t pv_smem_bytes(const PvParams& p);
