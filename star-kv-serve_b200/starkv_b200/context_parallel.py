@@ -20,6 +20,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+from .collectives import all_gather_into_
 
 _PACK = 130   # floats per (sequence, head): 128 output values, max, denominator
 
@@ -65,7 +66,7 @@ def gather_partials(out: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=N
     gathered = _gather_bufs.get(key)
     if gathered is None:
         gathered = _gather_bufs[key] = torch.empty(world * local.numel(), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(gathered, local, group=group)
+    all_gather_into_(gathered, local, group=group)
     return gathered
 
 

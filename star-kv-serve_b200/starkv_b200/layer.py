@@ -24,6 +24,7 @@ import torch
 import torch.nn.functional as F
 
 from . import context_parallel, sharding
+from .collectives import all_reduce_
 from .kernels import paged_quant as pq
 from .kernels.paged_decode import paged_starkv_decode, write_kv_bf16
 
@@ -210,8 +211,7 @@ class StarKVAttentionLayer:
     def _o_proj(self, attn: torch.Tensor, reduce: bool) -> torch.Tensor:
         out = F.linear(attn.to(self.wo.dtype), self.wo)
         if self.world > 1 and reduce:
-            import torch.distributed as dist
-            dist.all_reduce(out, group=self.group)
+            all_reduce_(out, group=self.group)
         return out
 
     def prefill(self, hidden: torch.Tensor, positions: torch.Tensor, prompt_lens: list[int], cache: torch.Tensor,

@@ -28,6 +28,7 @@ import torch
 import torch.nn.functional as F
 
 from . import sharding
+from .collectives import all_reduce_
 from .layer import HEAD_DIM, AttnWeights, StarKVAttentionLayer, StarKVContextLayer, rope
 from .workload import rope_cos_sin
 
@@ -114,8 +115,7 @@ class StockAttentionLayer:
                                block_table, seq_lens, 16, max_seq_len, None, "auto", self.one, self.one)
         o = F.linear(out.view(n, -1), self.wo)
         if self.world > 1 and reduce:
-            import torch.distributed as dist
-            dist.all_reduce(o, group=self.group)
+            all_reduce_(o, group=self.group)
         return o
 
 
@@ -231,8 +231,7 @@ class StarKVModel:
 
     def _all_reduce(self, x):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(x, group=self.group)
+            all_reduce_(x, group=self.group)
         return x
 
     def decode_step(self, tokens, positions, caches, block_table, seq_lens, max_seq_len, slot_mapping, ws=None,

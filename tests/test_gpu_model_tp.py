@@ -2,8 +2,8 @@
 NCCL ranks decode the small model sharded (heads LPT / even, MLP columns, o_proj and
 down_proj all-reduced) and get the unsharded model's logits. With the page split
 (attn_parallel="context") the compressed layers instead keep page p of every
-sequence on rank p % 2 and combine the ranks' partials. Needs two GPUs (run as
-child processes; skipped on one GPU)."""
+sequence on rank p % 2 and combine the ranks' partials. The NCCL form needs two
+GPUs (child processes); a gloo form runs both ranks on one GPU."""
 import os
 import socket
 
@@ -47,17 +47,20 @@ def _decode(model, dev):
     return logits
 
 
-def _worker(rank, port, quant, split, q):
+def _worker(rank, port, quant, split, q, one_gpu=False):
     import sys
     from datetime import timedelta
     import torch.distributed as dist
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "star-kv-serve_b200"))
     from starkv_b200.model import ModelConfig, StarKVModel
-    dev = torch.device("cuda", rank)
+    dev = torch.device("cuda", 0 if one_gpu else rank)
     torch.cuda.set_device(dev)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev, timeout=timedelta(seconds=60))
+    if one_gpu:   # both ranks on one GPU: gloo (the library stages its collectives through host memory)
+        dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=120))
+    else:
+        dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev, timeout=timedelta(seconds=60))
     try:
         cfg = dict(hidden=512, heads=4, ffn=1024, vocab=512, layers=3, full_layers=(0,), max_pos=256, seed=5)
         tp = _decode(StarKVModel(ModelConfig(**cfg), dev, quant=quant, rank=rank, world=2, attn_parallel=split),
@@ -71,22 +74,26 @@ def _worker(rank, port, quant, split, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("split", ["heads", "context"])
-@pytest.mark.parametrize("quant", [False, True])
-def test_model_tp2_matches_single_gpu(quant, split):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run_two_ranks(quant, split, one_gpu):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, quant, split, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, quant, split, q, one_gpu)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    rel = q.get(timeout=5)
+    return q.get(timeout=5)
+
+
+@pytest.mark.parametrize("split", ["heads", "context"])
+@pytest.mark.parametrize("quant", [False, True])
+def test_model_tp2_matches_single_gpu(quant, split):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    rel = _run_two_ranks(quant, split, one_gpu=False)
     print(f"{split} split, {'3.2-bit' if quant else 'bf16'}: relative logit difference {rel:.3e}")
     # bf16: only the rounding of the all-reduced partial sums differs. 3.2-bit: the
     # same, but a hidden state that differs by a bf16 rounding can move a code to
@@ -94,3 +101,15 @@ def test_model_tp2_matches_single_gpu(quant, split):
     # caches (every head's own codes and scales are identical between the splits)
     bound = 6e-2 if quant else 2e-2
     assert rel < bound, f"relative logit difference {rel:.3e}"
+
+
+@pytest.mark.parametrize("split", ["heads", "context"])
+def test_model_two_ranks_on_one_gpu_match_whole_model(split):
+    """The same two-rank model (bf16) with both ranks on one GPU over gloo: the
+    head-sharded and page-split layers, their all-reduces and the partials'
+    all-gather (staged through host memory), against the unsharded model. Runs
+    where only one GPU is present; the NCCL form above needs two."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    rel = _run_two_ranks(False, split, one_gpu=True)
+    assert rel < 2e-2, f"relative logit difference {rel:.3e}"
