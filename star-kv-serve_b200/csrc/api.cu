@@ -6,6 +6,7 @@
 //   fold_kernel -> scores_kernel (tcgen05) -> pv_kernel (tcgen05) -> lift_kernel
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <mutex>
 
 #include "starkv_common.cuh"
@@ -323,8 +324,31 @@ static int decode_impl(const StarKVDecodeArgs* a, void* workspace, size_t ws_byt
                        CU_TENSOR_MAP_SWIZZLE_NONE)))
       return st;
     if ((st = launch_pvq(tm_vq, tm_e, pp, dev.sms, stream))) return st;
-  } else if ((st = launch_pv(tm_v, tm_e, pp, dev.sms, stream))) {
-    return st;
+  } else {
+    // whole 64-channel V tiles of a page in one 4D box {64 channels, 16 slots, tiles,
+    // 1 block} over the V part of the rows (tile stride 128 B): one TMA request per
+    // page instead of one per tile, which the copy engine serves at a far higher rate
+    pp.v_full = a->v_rank / 64;
+    pp.v_tail = a->v_rank % 64 != 0;
+    pp.box_a = pp.n_ranges > 1 ? 2 * pp.mt_per_range : 0;
+    pp.box_b = pp.v_full - 2 * pp.mt_per_range * (pp.n_ranges - 1);
+    CUtensorMap tm_va{}, tm_vb{};
+    const uint64_t dims[4] = {64, (uint64_t)a->block_size, (uint64_t)std::max(pp.v_full, 1), (uint64_t)a->num_blocks};
+    const uint64_t str[3] = {(uint64_t)a->cache_stride[1] * es, 128, (uint64_t)a->cache_stride[0] * es};
+    const uint8_t* v_base = static_cast<const uint8_t*>(a->kv_cache) + (size_t)a->k_width * es;
+    if (pp.box_a > 0) {
+      const uint32_t box[4] = {64, 16, (uint32_t)pp.box_a, 1};
+      if ((st = make_map(&tm_va, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, v_base, dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    }
+    if (pp.box_b > 0) {
+      const uint32_t box[4] = {64, 16, (uint32_t)pp.box_b, 1};
+      if ((st = make_map(&tm_vb, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, v_base, dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    }
+    if ((st = launch_pv(tm_v, tm_va, tm_vb, tm_e, pp, dev.sms, stream))) return st;
   }
   if (pev) cudaEventRecord(pev[3], stream);
 

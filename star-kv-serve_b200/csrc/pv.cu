@@ -9,7 +9,8 @@
 // tcgen05 in swap-AB form, D[c, h] += V^T[c, t] . P^T[t, h]: M = 128 code
 // channels, N = heads (rounded to 16), K = 16 tokens (one page) per instruction,
 // f32 accumulators in TMEM across the whole token range. A = V^T straight from
-// the TMA page tile (MN-major, 128 B swizzle); P = e16 * exp(m_tile - m_seq) is
+// the TMA page tile (MN-major, 128 B swizzle; all whole 64-channel tiles of a page
+// in one 4D box); P = e16 * exp(m_tile - m_seq) is
 // built per page by the worker warps.
 //
 // Work split: the pages of all sequences are concatenated and cut into equal
@@ -33,6 +34,7 @@ using namespace pvc;
 namespace {
 
 constexpr int kMaxStages = 4;
+constexpr int kPageStages = 3;
 constexpr int kWorkers = 12;                 // worker warps (3 per TMEM lane quarter)
 constexpr int kWorkerThreads = 32 * kWorkers;
 constexpr int kIssuer2 = 2 + kWorkers;       // warp index of the second MMA issuer
@@ -61,8 +63,10 @@ __host__ __device__ inline PvLayout pv_layout(const PvParams& p) {
   L.e_bytes = (p.num_heads * 32 + 127) & ~127;
   L.p_bytes = p.nh * 32;
   L.stage_bytes = (L.v_bytes + L.e_bytes + L.p_bytes + 1023) & ~1023;
+  // three pages in flight: a fourth measured slower (more bytes outstanding per SM
+  // than the memory system serves best)
   int s = (200 * 1024) / L.stage_bytes;
-  L.stages = s > kMaxStages ? kMaxStages : s;
+  L.stages = s > kPageStages ? kPageStages : s;
   L.total = L.stages * L.stage_bytes + (int)sizeof(PvCtl) + 1024 + 64;
   return L;
 }
@@ -76,6 +80,8 @@ size_t pv_smem_bytes(const PvParams& p) {
 }
 
 __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant__ CUtensorMap tm_v,
+                                                    const __grid_constant__ CUtensorMap tm_va,
+                                                    const __grid_constant__ CUtensorMap tm_vb,
                                                     const __grid_constant__ CUtensorMap tm_e, const PvParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -119,6 +125,8 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     // the copies.
     if (lane == 0) {
       tma_prefetch(&tm_v);
+      if (p.box_a > 0) tma_prefetch(&tm_va);
+      if (p.box_b > 0) tma_prefetch(&tm_vb);
       tma_prefetch(&tm_e);
     }
     const int e_bytes = p.num_heads * 32;
@@ -139,7 +147,10 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
     bool stop = false;
     while (!stop && next_sub(u, u_end, total_pages, pprefix, pbeg, p.n, si)) {
       const int mt0 = si.range * p.mt_per_range;
-      const int mt1 = min(mt0 + p.mt_per_range, p.n_mtiles);
+      const bool last_range = si.range == p.n_ranges - 1;
+      const int nfull = last_range ? p.box_b : p.box_a;          // whole 64-channel tiles, one 4D box
+      const bool tail = last_range && p.v_tail;                   // + the trailing 32-channel tile
+      const uint32_t stage_tx = (nfull + (tail ? 1 : 0)) * 2048 + e_bytes;
       const int pend = si.page0 + si.npages;
       int ids_cur = block_of(si.b, si.page0 + lane, pend);
       int ids_nxt = block_of(si.b, si.page0 + 32 + lane, pend);
@@ -157,11 +168,13 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
             const int t = (si.page0 + pg) * 16;
             const int slot = t % p.block_size;
             uint8_t* st = smem + s * LY.stage_bytes;
-            mbar_arrive_expect_tx(&ctl->vfull[s], (mt1 - mt0) * 4096 + e_bytes);
-            for (int m = mt0; m < mt1; ++m)
-              for (int i = 0; i < 2; ++i)
-                tma_load_3d(st + (m - mt0) * 4096 + i * 2048, &tm_v, &ctl->vfull[s], p.k_width + m * 128 + 64 * i,
-                            slot, blk);
+            // tiles past the tail are not loaded: they only feed accumulator rows of
+            // channels >= v_rank, which are never flushed
+            mbar_arrive_expect_tx(&ctl->vfull[s], stage_tx);
+            if (nfull > 0) tma_load_4d(st, last_range ? &tm_vb : &tm_va, &ctl->vfull[s], 0, slot, 2 * mt0, blk);
+            if (tail)
+              tma_load_3d(st + (p.v_full - 2 * mt0) * 2048, &tm_v, &ctl->vfull[s], p.k_width + 64 * p.v_full, slot,
+                          blk);
             // e16 rows of this sequence's heads for the page's 16 tokens
             tma_load_2d(st + LY.v_bytes, &tm_e, &ctl->vfull[s], t, si.b * p.num_heads);
           }
@@ -342,14 +355,16 @@ __global__ void __launch_bounds__(kPvThreads, 1) pv_kernel(const __grid_constant
   }
 }
 
-int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms, cudaStream_t stream) {
+int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_va, const CUtensorMap& tm_vb, const CUtensorMap& tm_e,
+              const PvParams& p, int num_sms, cudaStream_t stream) {
   const PvLayout L = pv_layout(p);
   if (L.stages < 2) return STARKV_EINVAL;
   const size_t smem = pv_smem_bytes(p);
   if (smem > 227 * 1024) return STARKV_EINVAL;
   if (cudaFuncSetAttribute(pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return STARKV_ECUDA;
-  pv_kernel<<<num_sms, kPvThreads, smem, stream>>>(tm_v, tm_e, p);
+  if (p.box_a < 0 || p.box_b < 0 || p.box_a > 256 || p.box_b > 256) return STARKV_EINVAL;
+  pv_kernel<<<num_sms, kPvThreads, smem, stream>>>(tm_v, tm_va, tm_vb, tm_e, p);
   return cudaGetLastError() == cudaSuccess ? STARKV_OK : STARKV_ECUDA;
 }
 

@@ -67,6 +67,10 @@ struct PvParams {
   int v_pitch;            // 3.2-bit: staged row pitch of the V window [vx0, vq_off + v_bytes), odd x 16 B
   int cp_rank, cp_world;  // context split, as in ScoresParams (pages of the rank's 256-token tiles)
   int t_out;              // tiles over the outlier block (the rest cover inliers)
+  // bf16 / f16 V tiles: v_rank / 64 whole 64-channel tiles come in one 4D box per page
+  // (box_a tiles for every range but the last, box_b for the last one); a trailing
+  // 32-channel tile (v_tail) comes in a 3D box of its own
+  int v_full, box_a, box_b, v_tail;
   const __half* e16;
   const float* m_tile;
   const float* m_seq;
@@ -122,7 +126,8 @@ int launch_fold(const FoldParams& p, bool quant, cudaStream_t stream);
 int launch_scores(bool quant, const CUtensorMap& tm_cs, const CUtensorMap& tm_ab, const CUtensorMap& tm_code,
                   const CUtensorMap& tm_tail, const CUtensorMap& tm_sc, const ScoresParams& p, int num_sms,
                   cudaStream_t stream);
-int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_e, const PvParams& p, int num_sms, cudaStream_t stream);
+int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_va, const CUtensorMap& tm_vb, const CUtensorMap& tm_e,
+              const PvParams& p, int num_sms, cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
 int launch_lift_cluster(const LiftParams& p, cudaStream_t stream);   // -1: layout not taken
 
