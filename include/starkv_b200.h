@@ -194,6 +194,29 @@ STARKV_API int starkv_fold_q(const void* query, const int64_t q_stride[3], int32
                   const int32_t* head_of_lane, int32_t n, int32_t num_heads, int32_t k_width,
                   float scale, void* ab_out, int32_t* status, void* stream);
 
+/*
+ * attention.py:246-250 (flash_attn_varlen_func in _dense_prefill): causal attention
+ * of whole prompts over their own keys. Prompt p holds tokens
+ * cu_seqlens[p] .. cu_seqlens[p+1] (device int32, n_prompts + 1 entries) of
+ *   q   [T, num_heads, 128]      rotated queries
+ *   k   [T, num_k_heads, 128]    lifted, rotated keys (query head h reads K head
+ *                                h / (num_heads / num_k_heads))
+ *   v   [T, num_v_heads, 128]    lifted values (num_v_heads = num_heads: one V per
+ *                                query head; = num_k_heads: per KV head)
+ * -> out [T, num_heads, 128] = softmax(scale q k^T, key <= query) v.
+ * Strides are in elements, {token, head}; the last dimension is contiguous and the
+ * pointers and strides give 16-byte aligned rows. q, k, v and out share one dtype,
+ * STARKV_BF16 or STARKV_F16 (else STARKV_EDTYPE). q_tiles = sum over prompts of
+ * ceil(len / 128) (the grid; the kernel finds each tile's prompt in cu_seqlens).
+ * A cu_seqlens entry outside [0, T] is recorded as STARKV_EBOUNDS in *status
+ * (optional device int32).
+ */
+STARKV_API int starkv_prefill_attention(const void* q, const int64_t q_stride[2], const void* k,
+                  const int64_t k_stride[2], const void* v, const int64_t v_stride[2], int32_t dtype,
+                  int32_t num_tokens, int32_t num_heads, int32_t num_k_heads, int32_t num_v_heads,
+                  const int32_t* cu_seqlens, int32_t n_prompts, int32_t q_tiles, float scale, void* out,
+                  const int64_t o_stride[2], int32_t* status, void* stream);
+
 /* paged_quant.py:205-216 (pack_kv): quantize n tokens' codes into their slots. */
 typedef struct StarKVPackArgs {
   const void* k_codes; int64_t k_stride0; int32_t k_dtype;   /* [n, k_width], unit inner stride */

@@ -427,6 +427,47 @@ int starkv_fold_q(const void* query, const int64_t q_stride[3], int32_t q_dtype,
   return launch_fold(fp, true, (cudaStream_t)stream);
 }
 
+int starkv_prefill_attention(const void* q, const int64_t q_stride[2], const void* k, const int64_t k_stride[2],
+                             const void* v, const int64_t v_stride[2], int32_t dtype, int32_t num_tokens,
+                             int32_t num_heads, int32_t num_k_heads, int32_t num_v_heads, const int32_t* cu_seqlens,
+                             int32_t n_prompts, int32_t q_tiles, float scale, void* out, const int64_t o_stride[2],
+                             int32_t* status, void* stream) {
+  using namespace starkv;
+  if (!q || !k || !v || !out || !cu_seqlens || !q_stride || !k_stride || !v_stride || !o_stride || num_tokens < 0 ||
+      n_prompts < 0 || q_tiles < 0 || num_heads <= 0 || num_k_heads <= 0 || num_v_heads <= 0 ||
+      num_heads % num_k_heads || num_heads % num_v_heads)
+    return STARKV_EINVAL;
+  if (dtype != STARKV_BF16 && dtype != STARKV_F16) return STARKV_EDTYPE;
+  if (num_tokens == 0 || n_prompts == 0 || q_tiles == 0) return STARKV_OK;
+  const int64_t* strides[4] = {q_stride, k_stride, v_stride, o_stride};
+  for (const int64_t* s : strides)
+    if (s[0] <= 0 || s[1] <= 0 || s[0] % 8 || s[1] % 8) return STARKV_EALIGN;
+  for (const void* ptr : {q, k, v, (const void*)out})
+    if (reinterpret_cast<uintptr_t>(ptr) & 15) return STARKV_EALIGN;
+  DeviceInfo dev;
+  if (const int st = device_info(dev)) return st;
+  // one 3D map per operand: {128 dims, heads, tokens}, box {64 dims, 1 head, 128
+  // tokens}, 128-byte swizzle (the MMA operand layout); tokens past T read as zero
+  CUtensorMap maps[3];
+  const void* bases[3] = {q, k, v};
+  const int heads[3] = {num_heads, num_k_heads, num_v_heads};
+  for (int i = 0; i < 3; ++i) {
+    const uint64_t dims[3] = {128, (uint64_t)heads[i], (uint64_t)num_tokens};
+    const uint64_t str[2] = {(uint64_t)strides[i][1] * 2, (uint64_t)strides[i][0] * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    if (const int st = make_map(&maps[i], dtype == STARKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                3, bases[i], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+  }
+  PrefillParams pp{};
+  pp.cu_seqlens = cu_seqlens; pp.n_prompts = n_prompts; pp.num_tokens = num_tokens;
+  pp.num_heads = num_heads; pp.k_group = num_heads / num_k_heads; pp.v_group = num_heads / num_v_heads;
+  pp.dtype = dtype; pp.scale_log2 = scale * 1.4426950408889634f;
+  pp.out = out; pp.o_s0 = o_stride[0]; pp.o_s1 = o_stride[1]; pp.status = status;
+  return launch_prefill(maps[0], maps[1], maps[2], pp, q_tiles, (cudaStream_t)stream);
+}
+
 int starkv_read_status(void* workspace, int32_t* host_status, int32_t reset, void* stream) {
   if (!workspace || !host_status) return STARKV_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;

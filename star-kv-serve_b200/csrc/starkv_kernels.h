@@ -111,6 +111,17 @@ struct FoldParams {
   int32_t* status;
 };
 
+struct PrefillParams {
+  const int32_t* cu_seqlens;       // [n_prompts + 1] token offsets of the prompts
+  int n_prompts, num_tokens;
+  int num_heads;                   // query heads (grid.y)
+  int k_group, v_group;            // query heads per K head / per V head
+  int dtype;                       // STARKV_BF16 or STARKV_F16 (q, k, v and out)
+  float scale_log2;                // softmax scale * log2(e)
+  void* out; int64_t o_s0, o_s1;   // [T, num_heads, 128], strides in elements
+  int32_t* status;
+};
+
 size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch,
                          bool parts);
 int code_pitch_bytes(int bytes);
@@ -130,5 +141,7 @@ int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_va, const CUtensorM
               const PvParams& p, int num_sms, cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
 int launch_lift_cluster(const LiftParams& p, cudaStream_t stream);   // -1: layout not taken
+int launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PrefillParams& p,
+                   int q_tiles, cudaStream_t stream);
 
 }  // namespace starkv

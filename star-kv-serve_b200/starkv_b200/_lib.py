@@ -88,6 +88,8 @@ EXPORTS = {
     "starkv_selftest_wait_timeout": (C.c_int, [p, p]),
     "starkv_fold_q": (C.c_int, [p, C.POINTER(i64), i32, p, C.POINTER(i64), i32, p, i32, i32, i32, f32, p, p, p]),
     "starkv_pack_kv_q32": (C.c_int, [C.POINTER(PackArgs), p]),
+    "starkv_prefill_attention": (C.c_int, [p, C.POINTER(i64), p, C.POINTER(i64), p, C.POINTER(i64), i32, i32, i32, i32,
+                                           i32, p, i32, i32, f32, p, C.POINTER(i64), p, p]),
     "starkv_cache_write_bf16": (C.c_int, [C.POINTER(CacheWriteArgs), p]),
     "starkv_read_status": (C.c_int, [p, C.POINTER(i32), i32, p]),
     "starkv_status_offset": (C.c_size_t, []),

@@ -27,6 +27,7 @@ from . import context_parallel, sharding
 from .collectives import all_reduce_
 from .kernels import paged_quant as pq
 from .kernels.paged_decode import paged_starkv_decode, write_kv_bf16
+from .kernels.prefill import prefill_attention
 
 HEAD_DIM = 128
 
@@ -220,12 +221,13 @@ class StarKVAttentionLayer:
         (attention.py:219-251): every prompt token's codes are written / packed at
         `slot_mapping`, K is lifted per head from this step's own codes with one
         bmm and rotated, V lifted by v_up, and each prompt attends causally over
-        itself (torch SDPA). hidden [T, hidden] holds the prompts back to back
+        itself (the library's prefill attention kernel, in place of the reference's
+        flash_attn_varlen_func). hidden [T, hidden] holds the prompts back to back
         (`prompt_lens`), `positions` their positions; returns o_proj [T, hidden]."""
         T = hidden.shape[0]
         if sum(prompt_lens) != T:
             raise ValueError("prompt_lens must cover the T tokens of hidden")
-        H, G = self.num_kv_heads, self.num_heads // self.num_kv_heads
+        H = self.num_kv_heads
         q = rope(F.linear(hidden, self.wq).view(T, self.num_heads, HEAD_DIM), positions, self.cos_sin_cache)
         kc, vc = self.codes(hidden)
         if self.quant:
@@ -237,16 +239,10 @@ class StarKVAttentionLayer:
         # V per query head: v_codes . v_up_by_q[hq] (the heads of a KV group share one
         # v_up in a checkpoint, attention.py:158-160, but nothing here relies on it)
         v = torch.einsum("tr,hrd->thd", vc, self.v_up_by_q)
-        out = torch.empty(T, self.num_heads, HEAD_DIM, dtype=q.dtype, device=q.device)
-        s0 = 0
-        for L in prompt_lens:
-            qs = q[s0:s0 + L].transpose(0, 1)                                   # [Hq, L, Hd]
-            ks = k[s0:s0 + L].transpose(0, 1).repeat_interleave(G, dim=0)     # [Hq, L, Hd]
-            vs = v[s0:s0 + L].transpose(0, 1)
-            out[s0:s0 + L] = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True,
-                                                            scale=self.scale).transpose(0, 1)
-            s0 += L
-        return self._o_proj(out.reshape(T, -1), reduce)
+        dt = q.dtype if q.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+        out = prefill_attention(q.to(dt).contiguous(), k.to(dt).contiguous(), v.to(dt).contiguous(), prompt_lens,
+                                self.scale)
+        return self._o_proj(out.to(q.dtype).reshape(T, -1), reduce)
 
 
 class StarKVContextLayer(StarKVAttentionLayer):

@@ -89,6 +89,14 @@ def test_entry_points_reject_bad_arguments_before_any_gpu_work(lib):
     assert lib.starkv_fold_q(fake, qs, _lib.BF16, fake, us, 9, fake, 2, 32, 64, 0.1, fake, None, None) == 101
     assert lib.starkv_fold_q(fake, qs, _lib.BF16, fake, us, _lib.BF16, fake, 2, 32, 40, 0.1, fake, None, None) == 22
     assert lib.starkv_fold_q(None, qs, _lib.BF16, fake, us, _lib.BF16, fake, 2, 32, 64, 0.1, fake, None, None) == 22
+    # prefill attention: pointers, head counts, dtype and alignment are checked first
+    s2 = _lib.i64s([4096, 128])
+    pa = lambda q, dt, H, Hk, Hv, st=s2: lib.starkv_prefill_attention(  # noqa: E731
+        q, st, fake, s2, fake, s2, dt, 100, H, Hk, Hv, fake, 2, 1, 0.1, fake, s2, None, None)
+    assert pa(None, _lib.BF16, 32, 8, 32) == 22
+    assert pa(fake, _lib.BF16, 32, 5, 32) == 22          # 32 query heads over 5 K heads
+    assert pa(fake, _lib.F32, 32, 8, 32) == 101
+    assert pa(fake, _lib.BF16, 32, 8, 32, _lib.i64s([4100, 128])) == 100   # row stride not 16-byte aligned
 
 
 def test_quant_row_matches_oracle():
