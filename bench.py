@@ -515,6 +515,56 @@ def model_measure(args, device, world, rank, dist_on, parallel, batch=None, cont
             "data": "synthetic (seeded caches)"}
 
 
+def prefill_measure(device, steps, warmup, tf_peak, peak_kind):
+    """Dense prefill attention (the reference prefill's flash_attn_varlen_func,
+    attention.py:246-250) on the library's kernel: 8 prompts x 2048 tokens, 32 heads
+    x 128, bf16, causal; beside it the same call through flash_attn (the reference's
+    library) and torch SDPA when they run here."""
+    import torch
+    from starkv_b200.kernels.prefill import cu_seqlens_of, prefill_attention
+    lens, H = [2048] * 8, 32
+    T = sum(lens)
+    g = torch.Generator(device=device).manual_seed(7)
+    q, k, v = (torch.randn(T, H, 128, generator=g, device=device).to(torch.bfloat16) for _ in range(3))
+    cu = cu_seqlens_of(lens, device)
+    scale = 128 ** -0.5
+    flops = 4 * 128 * H * sum(L * (L + 1) // 2 for L in lens)
+    out = torch.empty_like(q)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(lambda: prefill_attention(q, k, v, lens, scale, cu_seqlens=cu, out=out))
+    res = {"workload": "dense prefill attention: 8 prompts x 2048 tokens, 32 heads x 128, bf16, causal",
+           "ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+           "roofline": {"bound": "tensor", "achieved": round(flops / (ms * 1e-3) / 1e12, 1), "peak": tf_peak,
+                        "unit": "TFLOP/s", "frac": round(flops / (ms * 1e-3) / 1e12 / tf_peak, 4),
+                        "peak_kind": peak_kind},
+           "l2": "inputs 100 MB; compute-bound"}
+    try:
+        from flash_attn import flash_attn_varlen_func
+        fa = timed(lambda: flash_attn_varlen_func(q, k, v, cu, cu, 2048, 2048, softmax_scale=scale, causal=True))
+        res["flash_attn_ms"] = round(fa, 4)
+    except Exception as e:   # noqa: BLE001 - the comparison is optional
+        res["flash_attn_ms"] = f"unavailable: {type(e).__name__}"
+    try:
+        qs, ks, vs = (x.view(8, 2048, H, 128).transpose(1, 2) for x in (q, k, v))
+        sd = timed(lambda: torch.nn.functional.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=scale))
+        res["torch_sdpa_ms"] = round(sd, 4)
+    except Exception as e:   # noqa: BLE001
+        res["torch_sdpa_ms"] = f"unavailable: {type(e).__name__}"
+    return res
+
+
 def rank_tokens(layer, cp):
     """Tokens this rank decodes: all, or its share of each sequence's 256-token tiles."""
     if cp is None:
@@ -769,7 +819,11 @@ def ours(args):
             dist.barrier()
             dist.destroy_process_group()
         return
-    if args.case == "c4":
+    if args.case == "prefill":
+        if rank == 0:
+            print(json.dumps({"case": "prefill", **prefill_measure(device, args.steps, args.warmup, tf_peak,
+                                                                   peak_kind)}), flush=True)
+    elif args.case == "c4":
         # config 4 alone (mixed lengths, skewed ranks), both formats: one line, no baselines
         c4 = {key: decode_case(quant, True, args, world, rank, device, dist_on, hbm_peak)
               for quant, key in ((False, "bf16"), (True, "q32"))}
@@ -799,6 +853,9 @@ def ours(args):
         model = None
         if "model" not in args.skip:
             model = model_measure(args, device, world, rank, dist_on, args.parallel)
+        prefill = None
+        if world == 1 and "prefill" not in args.skip:
+            prefill = prefill_measure(device, max(args.steps, 5), max(args.warmup, 3), tf_peak, peak_kind)
         if rank == 0:
             reps = world if dist_on and args.parallel == "seqs" else 1   # batches in the job (seqs: one per GPU)
             cpu_line = cpu_baseline_line() if world == 1 else None
@@ -840,6 +897,8 @@ def ours(args):
                 line["c4"] = c4_summary(c4, args.parallel, world, hbm_peak)
             if model is not None:
                 line["model"] = model
+            if prefill is not None:
+                line["prefill"] = prefill
             if cpu_line is not None:
                 line["cpu_baseline"] = cpu_line
             print(json.dumps(line), flush=True)
@@ -935,14 +994,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4", "layer", "model"],
+    ap.add_argument("--case", default="both", choices=["both", "c2", "c3", "c4", "layer", "model", "prefill"],
                     help="c2 / c3 alone: one configuration, short output (profiling)")
     ap.add_argument("--parallel", default="context", choices=["seqs", "context", "heads"],
                     help="N > 1: one batch split over the GPUs by each sequence's tiles (context, default; the "
                          "head split is measured beside it), or by heads; or a batch of sequences per GPU (seqs, "
                          "weak scaling)")
     ap.add_argument("--skip", default="", help="comma list of parts of the default run to leave out: "
-                                               "heads, c4, model, bar")
+                                               "heads, c4, model, bar, prefill")
     ap.add_argument("--model-weights", default="checkpoint", choices=["checkpoint", "random"],
                     help="config 5: K/V factors from a synthetic fused_weights.pt (default) or drawn in place")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling small cases)")

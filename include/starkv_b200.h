@@ -206,7 +206,7 @@ STARKV_API int starkv_fold_q(const void* query, const int64_t q_stride[3], int32
  * -> out [T, num_heads, 128] = softmax(scale q k^T, key <= query) v.
  * Strides are in elements, {token, head}; the last dimension is contiguous and the
  * pointers and strides give 16-byte aligned rows. q, k, v and out share one dtype,
- * STARKV_BF16 or STARKV_F16 (else STARKV_EDTYPE). q_tiles = sum over prompts of
+ * STARKV_BF16 or STARKV_F16 (else STARKV_EDTYPE); scale > 0. q_tiles = sum over prompts of
  * ceil(len / 128) (the grid; the kernel finds each tile's prompt in cu_seqlens).
  * A cu_seqlens entry outside [0, T] is recorded as STARKV_EBOUNDS in *status
  * (optional device int32).

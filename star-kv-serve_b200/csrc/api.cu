@@ -435,7 +435,7 @@ int starkv_prefill_attention(const void* q, const int64_t q_stride[2], const voi
   using namespace starkv;
   if (!q || !k || !v || !out || !cu_seqlens || !q_stride || !k_stride || !v_stride || !o_stride || num_tokens < 0 ||
       n_prompts < 0 || q_tiles < 0 || num_heads <= 0 || num_k_heads <= 0 || num_v_heads <= 0 ||
-      num_heads % num_k_heads || num_heads % num_v_heads)
+      num_heads % num_k_heads || num_heads % num_v_heads || !(scale > 0.f))
     return STARKV_EINVAL;
   if (dtype != STARKV_BF16 && dtype != STARKV_F16) return STARKV_EDTYPE;
   if (num_tokens == 0 || n_prompts == 0 || q_tiles == 0) return STARKV_OK;

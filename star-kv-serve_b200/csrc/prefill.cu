@@ -9,8 +9,9 @@
 //                         the softmax reads S_j;
 //   P_j = exp(S_j - m)    online softmax by 4 warps (one query row per thread, a
 //                         TMEM lane each), the running output rescaled in TMEM when
-//                         a row's max grows; P_j (bf16 / f16) written to shared
-//                         memory in the 128-byte-swizzled K-major MMA layout;
+//                         a row's max grows by more than 2^8; P_j (bf16 / f16)
+//                         written to shared memory in the 128-byte-swizzled K-major
+//                         MMA layout;
 //   O  += P_j . V_j       tcgen05 (N = 128 dims, K = 128 keys), f32 in TMEM.
 // Q, K and V tiles come by TMA (128-byte swizzle, two 64-dim boxes per tile); K / V
 // are double-buffered. The last tile is masked causally (key > query) and every
@@ -61,6 +62,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2^x by the hardware approximation (ex2.approx.ftz: -inf -> +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // Bounded wait that ignores the abort flag: used at teardown so that no copy or MMA
 // of this CTA is still writing its shared memory or TMEM when the CTA exits.
@@ -238,15 +246,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&ctl->s_free[s]);
         // keys of this tile a query may see: k <= qi and k < L
         const int kend = min(qi + 1, L) - kRows * j;   // valid columns [0, kend)
-        float mt = -INFINITY;
+        // masked logits become -inf (their exponentials 0); eight independent max and
+        // sum chains keep the pass from serialising on one accumulator
+        if (!__all_sync(0xffffffffu, kend >= kRows)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * c + i >= kend) sr[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (32 * c + i < kend) mt = fmaxf(mt, __uint_as_float(sr[c][i]) * p.scale_log2);
-        const float m_new = fmaxf(m, mt);
-        const float alpha = (m_new == -INFINITY || m == m_new) ? 1.f : exp2f(m - m_new);
-        float rs = 0.f;
+          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sr[c][i]));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], mx[e + 4]);
+        const float mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        const float mt = mraw * p.scale_log2;   // scale_log2 > 0
+        // The reference max m moves only when the tile max exceeds it by more than
+        // 2^8 (log2 units): P = exp2(s - m) <= 256 then, exact enough in f32 sums and
+        // bf16 / f16 P, and the output is rescaled far less often. The result is the
+        // same softmax: numerator and denominator share the reference.
+        const bool move = mt > m + 8.f;
+        const float m_new = move ? mt : m;
+        const float alpha = (move && m != -INFINITY) ? exp2f(m - m_new) : 1.f;
+        // exponentials before waiting for the previous P . V: they overlap its MMAs
+        float sum8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum8[e] = 0.f;
+        const float mneg = m_new == -INFINITY ? 0.f : -m_new;   // a row with no key yet: all -inf -> 0
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float pv = ex2_approx(fmaf(__uint_as_float(sr[c][i]), p.scale_log2, mneg));
+            sum8[i & 7] += pv;
+            sr[c][i] = __float_as_uint(pv);
+          }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sum8[e] += sum8[e + 4];
+        const float rs = (sum8[0] + sum8[1]) + (sum8[2] + sum8[3]);
+        l = l * alpha + rs;
+        m = m_new;
         // the previous P . V must be complete before P is overwritten and O rescaled
         if (j > 0 && !mbar_wait(&ctl->o_done, (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
@@ -256,21 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int g = 0; g < 4; ++g) {   // 8 keys = one 16-byte chunk
             uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int k0 = 32 * c + 8 * g + 2 * e;
-              const float p0 = k0 < kend ? exp2f(__uint_as_float(sr[c][8 * g + 2 * e]) * p.scale_log2 - m_new) : 0.f;
-              const float p1 =
-                  k0 + 1 < kend ? exp2f(__uint_as_float(sr[c][8 * g + 2 * e + 1]) * p.scale_log2 - m_new) : 0.f;
-              rs += p0 + p1;
-              w[e] = pack2<T>(p0, p1);
-            }
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack2<T>(__uint_as_float(sr[c][8 * g + 2 * e]), __uint_as_float(sr[c][8 * g + 2 * e + 1]));
             const int chunk = (4 * c + g) & 7, half = c >> 1;
             *reinterpret_cast<uint4*>(prow + half * kHalfBytes + ((chunk ^ (row & 7)) << 4)) =
                 make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        l = l * alpha + rs;
-        m = m_new;
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
           // rescale this warp's rows of the running output
 #pragma unroll
