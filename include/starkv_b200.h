@@ -217,6 +217,24 @@ STARKV_API int starkv_prefill_attention(const void* q, const int64_t q_stride[2]
                   const int32_t* cu_seqlens, int32_t n_prompts, int32_t q_tiles, float scale, void* out,
                   const int64_t o_stride[2], int32_t* status, void* stream);
 
+/*
+ * model.py:70 (codes = F.linear(hidden, kv_down)) fused with the cache write of
+ * attention.py:179-185: cache[slot_t] row [0, out_width) = hidden_t . kv_down^T for
+ * the n tokens, rounded once to the cache dtype, so the codes never go through
+ * global memory. hidden [n, hidden_dim] (row stride h_stride0 elements), kv_down
+ * [out_width, hidden_dim] (row stride w_stride0), both of `dtype` (STARKV_BF16 or
+ * STARKV_F16, as the cache; else STARKV_EDTYPE), last dimensions contiguous, rows
+ * 16-byte aligned; hidden_dim a multiple of 512; cache [num_blocks, block_size, >=
+ * out_width] with strides cache_stride (elements) multiples of 8. slot_mapping int32
+ * or int64 [n]; slot -1 (CUDA-graph padding) writes the reserved null slot 0, as
+ * attention.py:181 clamps it; a slot past the cache is recorded as STARKV_EBOUNDS
+ * in *status (optional device int32) and not written.
+ */
+STARKV_API int starkv_kv_down_cache_write(const void* hidden, int64_t h_stride0, const void* kv_down,
+                  int64_t w_stride0, int32_t dtype, int32_t n, int32_t hidden_dim, int32_t out_width,
+                  void* kv_cache, const int64_t cache_stride[2], int32_t num_blocks, int32_t block_size,
+                  const void* slot_mapping, int32_t slot_dtype, int32_t* status, void* stream);
+
 /* paged_quant.py:205-216 (pack_kv): quantize n tokens' codes into their slots. */
 typedef struct StarKVPackArgs {
   const void* k_codes; int64_t k_stride0; int32_t k_dtype;   /* [n, k_width], unit inner stride */

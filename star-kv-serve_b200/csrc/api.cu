@@ -468,6 +468,50 @@ int starkv_prefill_attention(const void* q, const int64_t q_stride[2], const voi
   return launch_prefill(maps[0], maps[1], maps[2], pp, q_tiles, (cudaStream_t)stream);
 }
 
+int starkv_kv_down_cache_write(const void* hidden, int64_t h_stride0, const void* kv_down, int64_t w_stride0,
+                               int32_t dtype, int32_t n, int32_t hidden_dim, int32_t out_width, void* kv_cache,
+                               const int64_t cache_stride[2], int32_t num_blocks, int32_t block_size,
+                               const void* slot_mapping, int32_t slot_dtype, int32_t* status, void* stream) {
+  using namespace starkv;
+  if (!hidden || !kv_down || !kv_cache || !cache_stride || !slot_mapping || n < 0 || out_width <= 0 ||
+      hidden_dim <= 0 || hidden_dim % (64 * kv_down_split()) || num_blocks <= 0 || block_size <= 0 ||
+      cache_stride[1] < out_width || cache_stride[0] < cache_stride[1] * block_size || h_stride0 < hidden_dim ||
+      w_stride0 < hidden_dim || (slot_dtype != STARKV_I32 && slot_dtype != STARKV_I64))
+    return STARKV_EINVAL;
+  if (dtype != STARKV_BF16 && dtype != STARKV_F16) return STARKV_EDTYPE;
+  if (h_stride0 % 8 || w_stride0 % 8 || cache_stride[0] % 8 || cache_stride[1] % 8) return STARKV_EALIGN;
+  for (const void* ptr : {hidden, kv_down, (const void*)kv_cache})
+    if (reinterpret_cast<uintptr_t>(ptr) & 15) return STARKV_EALIGN;
+  if (n == 0) return STARKV_OK;
+  DeviceInfo dev;
+  if (const int st = device_info(dev)) return st;
+  DownWriteParams dp{};
+  dp.n = n; dp.hidden = hidden_dim; dp.out_width = out_width;
+  dp.n_tile = std::min(256, (n + 15) / 16 * 16);
+  dp.stages = std::min(4, hidden_dim / (64 * kv_down_split()));
+  dp.ctl_offset = kv_down_ctl_offset(dp.n_tile, dp.stages);
+  dp.dtype = dtype; dp.cache = kv_cache; dp.c_s0 = cache_stride[0]; dp.c_s1 = cache_stride[1];
+  dp.num_blocks = num_blocks; dp.block_size = block_size; dp.slot_mapping = slot_mapping;
+  dp.slot_dtype = slot_dtype; dp.status = status;
+  const CUtensorMapDataType tdt = dtype == STARKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tm_w, tm_x;
+  {
+    // weight rows: box {64 hidden, 128 channels}, 128-byte swizzle; channels past out_width read as zero
+    const uint64_t dims[2] = {(uint64_t)hidden_dim, (uint64_t)out_width};
+    const uint64_t str[1] = {(uint64_t)w_stride0 * 2};
+    const uint32_t box[2] = {64, 128};
+    if (const int st = make_map(&tm_w, tdt, 2, kv_down, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  {
+    // token rows: box {64 hidden, n_tile tokens}; tokens past n read as zero
+    const uint64_t dims[2] = {(uint64_t)hidden_dim, (uint64_t)n};
+    const uint64_t str[1] = {(uint64_t)h_stride0 * 2};
+    const uint32_t box[2] = {64, (uint32_t)dp.n_tile};
+    if (const int st = make_map(&tm_x, tdt, 2, hidden, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  return launch_kv_down_write(tm_w, tm_x, dp, (cudaStream_t)stream);
+}
+
 int starkv_read_status(void* workspace, int32_t* host_status, int32_t reset, void* stream) {
   if (!workspace || !host_status) return STARKV_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;

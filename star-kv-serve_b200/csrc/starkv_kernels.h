@@ -122,6 +122,15 @@ struct PrefillParams {
   int32_t* status;
 };
 
+struct DownWriteParams {
+  int n, hidden, out_width;        // tokens, K, code channels (k_width + v_rank)
+  int n_tile, stages, ctl_offset;  // tokens per launch column (multiple of 16, <= 256), K-block ring
+  int dtype;                       // STARKV_BF16 or STARKV_F16 (hidden, kv_down and the cache)
+  void* cache; int64_t c_s0, c_s1; int num_blocks, block_size;   // strides in elements
+  const void* slot_mapping; int slot_dtype;
+  int32_t* status;
+};
+
 size_t scores_smem_bytes(bool quant, int num_kv_heads, int n, int k_width, int code_pitch, int sc_pitch,
                          bool parts);
 int code_pitch_bytes(int bytes);
@@ -141,6 +150,11 @@ int launch_pv(const CUtensorMap& tm_v, const CUtensorMap& tm_va, const CUtensorM
               const PvParams& p, int num_sms, cudaStream_t stream);
 int launch_lift(const LiftParams& p, cudaStream_t stream);
 int launch_lift_cluster(const LiftParams& p, cudaStream_t stream);   // -1: layout not taken
+size_t kv_down_smem_bytes(int n_tile, int stages);
+int kv_down_ctl_offset(int n_tile, int stages);
+int kv_down_split();
+int launch_kv_down_write(const CUtensorMap& tm_w, const CUtensorMap& tm_x, const DownWriteParams& p,
+                         cudaStream_t stream);
 int launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PrefillParams& p,
                    int q_tiles, cudaStream_t stream);
 

@@ -88,6 +88,8 @@ EXPORTS = {
     "starkv_selftest_wait_timeout": (C.c_int, [p, p]),
     "starkv_fold_q": (C.c_int, [p, C.POINTER(i64), i32, p, C.POINTER(i64), i32, p, i32, i32, i32, f32, p, p, p]),
     "starkv_pack_kv_q32": (C.c_int, [C.POINTER(PackArgs), p]),
+    "starkv_kv_down_cache_write": (C.c_int, [p, i64, p, i64, i32, i32, i32, i32, p, C.POINTER(i64), i32, i32, p, i32,
+                                             p, p]),
     "starkv_prefill_attention": (C.c_int, [p, C.POINTER(i64), p, C.POINTER(i64), p, C.POINTER(i64), i32, i32, i32, i32,
                                            i32, p, i32, i32, f32, p, C.POINTER(i64), p, p]),
     "starkv_cache_write_bf16": (C.c_int, [C.POINTER(CacheWriteArgs), p]),

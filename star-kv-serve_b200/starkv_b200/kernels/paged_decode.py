@@ -117,3 +117,25 @@ def write_kv_bf16(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor
     a.n, a.k_width, a.v_rank = n, key.shape[1], value.shape[1]
     a.status = None if status is None else status.data_ptr()
     _lib.check(_lib.lib().starkv_cache_write_bf16(a, _lib.stream_ptr(kv_cache.device)), "write_kv_bf16")
+
+
+def kv_down_write(hidden: torch.Tensor, kv_down: torch.Tensor, kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                  status: torch.Tensor | None = None) -> None:
+    """The step's codes straight into the cache: ``cache[slot] = hidden . kv_down^T``
+    (model.py:70 ``F.linear(hidden, kv_down)`` followed by the cache write of
+    attention.py:179-185, slot -1 sent to the null block), in one launch of the
+    library's fused GEMM + write kernel. hidden [n, hidden_dim], kv_down [W + rv,
+    hidden_dim], both in the cache's dtype (bf16 or f16); hidden_dim a multiple of 512."""
+    n = hidden.shape[0]
+    if n == 0:
+        return
+    if hidden.stride(-1) != 1 or kv_down.stride(-1) != 1:
+        raise ValueError("kv_down_write: hidden and kv_down need a contiguous last dimension")
+    if hidden.dtype != kv_cache.dtype or kv_down.dtype != kv_cache.dtype:
+        raise ValueError("kv_down_write: hidden, kv_down and the cache must share one dtype")
+    st = _lib.lib().starkv_kv_down_cache_write(
+        hidden.data_ptr(), hidden.stride(0), kv_down.data_ptr(), kv_down.stride(0), _lib.dtype_code(hidden), n,
+        hidden.shape[1], kv_down.shape[0], kv_cache.data_ptr(), _lib.i64s(kv_cache.stride()[:2]), kv_cache.shape[0],
+        kv_cache.shape[1], slot_mapping.data_ptr(), _lib.dtype_code(slot_mapping), _lib.ptr(status),
+        _lib.stream_ptr(kv_cache.device))
+    _lib.check(st, "kv_down_write")

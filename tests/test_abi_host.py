@@ -97,6 +97,15 @@ def test_entry_points_reject_bad_arguments_before_any_gpu_work(lib):
     assert pa(fake, _lib.BF16, 32, 5, 32) == 22          # 32 query heads over 5 K heads
     assert pa(fake, _lib.F32, 32, 8, 32) == 101
     assert pa(fake, _lib.BF16, 32, 8, 32, _lib.i64s([4100, 128])) == 100   # row stride not 16-byte aligned
+    # fused K/V down-projection + cache write: shapes, dtype and alignment first
+    cs = _lib.i64s([16 * 2928, 2928])
+    kd = lambda h, dt, hid, st=cs, hs=4096: lib.starkv_kv_down_cache_write(  # noqa: E731
+        h, hs, fake, 4096, dt, 64, hid, 2928, fake, st, 64, 16, fake, _lib.I32, None, None)
+    assert kd(None, _lib.BF16, 4096) == 22
+    assert kd(fake, _lib.BF16, 4000) == 22                 # hidden not a multiple of 512
+    assert kd(fake, _lib.F32, 4096) == 101
+    assert kd(fake, _lib.BF16, 4096, _lib.i64s([16 * 2928, 2000])) == 22    # cache row narrower than the codes
+    assert kd(fake, _lib.BF16, 4096, hs=4100) == 100        # hidden row stride not 16-byte aligned
 
 
 def test_quant_row_matches_oracle():
