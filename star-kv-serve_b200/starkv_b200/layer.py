@@ -26,7 +26,7 @@ import torch.nn.functional as F
 from . import context_parallel, sharding
 from .collectives import all_reduce_
 from .kernels import paged_quant as pq
-from .kernels.paged_decode import paged_starkv_decode, write_kv_bf16
+from .kernels.paged_decode import kv_down_write, paged_starkv_decode, write_kv_bf16
 from .kernels.prefill import prefill_attention
 
 HEAD_DIM = 128
@@ -193,21 +193,35 @@ class StarKVAttentionLayer:
         unless `reduce` is False (then this rank's partial sum)."""
         n = hidden.shape[0]
         q = rope(F.linear(hidden, self.wq).view(n, self.num_heads, HEAD_DIM), positions, self.cos_sin_cache)
-        k, v = self.codes(hidden)
         # CUDA-graph padding rows carry slot -1 (written to the reserved null block)
         # and length 0; as attention.py:199 does, they attend to one null-block position
         seq_lens = seq_lens.clamp(min=1)
         if self.quant:
+            k, v = self.codes(hidden)
             pq.pack_kv(k, v, cache, slot_mapping, self.row, self.k_ranks, self.k_head_offsets, self.k_nouts)
             attn = pq.paged_quant_decode(q, cache, block_table, seq_lens, max_seq_len, self.row, self.k_up,
                                          self.head_of_lane, self.k_tiles, self.v_up_by_q, self.cos_sin_cache,
                                          self.scale, ws=ws)
         else:
-            write_kv_bf16(k, v, cache, slot_mapping)
+            self._write_codes(hidden, cache, slot_mapping)
             attn = paged_starkv_decode(q, cache, block_table, seq_lens, max_seq_len, self.k_up, self.k_ranks,
                                        self.k_head_offsets, self.k_width, self.v_up_by_q, self.cos_sin_cache,
                                        self.scale, ws=ws)
         return self._o_proj(attn.reshape(n, -1), reduce)
+
+    def _write_codes(self, hidden: torch.Tensor, cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+        """bf16 / f16 cache: the step's codes go straight from the down-projection into
+        their cache rows (one fused launch) at decode batch sizes, where the weight read
+        is the cost (64 tokens, config-2 widths: 13.0 against 14.1 us for F.linear and
+        the cache-write kernel; 24 tokens 9.3 against 13.7 us); larger batches, where
+        the split-K reduction dominates (256 tokens: 33 against 15 us), and shapes the
+        kernel does not take go through F.linear and the cache-write kernel."""
+        if (hidden.shape[0] <= 128 and hidden.dtype == cache.dtype == self.kv_down.dtype
+                and hidden.shape[1] % 512 == 0 and hidden.stride(-1) == 1 and hidden.stride(0) % 8 == 0):
+            kv_down_write(hidden, self.kv_down, cache, slot_mapping)
+        else:
+            k, v = self.codes(hidden)
+            write_kv_bf16(k, v, cache, slot_mapping)
 
     def _o_proj(self, attn: torch.Tensor, reduce: bool) -> torch.Tensor:
         out = F.linear(attn.to(self.wo.dtype), self.wo)
@@ -271,13 +285,13 @@ class StarKVContextLayer(StarKVAttentionLayer):
         unnormalised, m [n, H], l [n, H])."""
         n = hidden.shape[0]
         q = rope(F.linear(hidden, self.wq).view(n, self.num_heads, HEAD_DIM), positions, self.cos_sin_cache)
-        k, v = self.codes(hidden)
         if self.quant:
+            k, v = self.codes(hidden)
             pq.pack_kv(k, v, cache, slot_mapping, self.row, self.k_ranks, self.k_head_offsets, self.k_nouts)
             return pq.paged_quant_decode(q, cache, block_table, seq_lens, max_seq_len, self.row, self.k_up,
                                          self.head_of_lane, self.k_tiles, self.v_up_by_q, self.local_cos_sin,
                                          self.scale, ws=ws, context=(0, 1))
-        write_kv_bf16(k, v, cache, slot_mapping)
+        self._write_codes(hidden, cache, slot_mapping)
         return paged_starkv_decode(q, cache, block_table, seq_lens, max_seq_len, self.k_up, self.k_ranks,
                                    self.k_head_offsets, self.k_width, self.v_up_by_q, self.local_cos_sin,
                                    self.scale, ws=ws, context=(0, 1))
