@@ -359,3 +359,33 @@ def rope_cos_sin(max_pos: int, head_dim: int = HEAD_DIM, base: float = 10000.0,
     pos = np.arange(max_pos, dtype=np.float64) / linear_factor
     fr = np.outer(pos, inv)
     return np.concatenate([np.cos(fr), np.sin(fr)], 1).astype(np.float32)
+
+
+def causal_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, prompt_lens, scale: float) -> np.ndarray:
+    """The attention of the reference's dense prefill (attention.py:246-250,
+    flash_attn_varlen_func with causal=True): prompts back to back in the token
+    dimension; query t of a prompt attends to the prompt's keys up to itself.
+    q [T, H, D], k [T, H_k, D], v [T, H_v, D] (query head h reads K head
+    h // (H / H_k) and V head h // (H / H_v)); returns [T, H, D] in float64."""
+    T, H, _ = q.shape
+    gk, gv = H // k.shape[1], H // v.shape[1]
+    out = np.zeros(q.shape, dtype=np.float64)
+    s0 = 0
+    for L in prompt_lens:
+        for h in range(H):
+            qs = q[s0:s0 + L, h].astype(np.float64)
+            ks = k[s0:s0 + L, h // gk].astype(np.float64)
+            vs = v[s0:s0 + L, h // gv].astype(np.float64)
+            s = scale * qs @ ks.T
+            s[np.triu_indices(L, 1)] = -np.inf
+            p = np.exp(s - s.max(axis=1, keepdims=True))
+            out[s0:s0 + L, h] = (p / p.sum(axis=1, keepdims=True)) @ vs
+        s0 += L
+    return out
+
+
+def code_rows(hidden: np.ndarray, kv_down: np.ndarray) -> np.ndarray:
+    """The step's cache rows before rounding: codes = F.linear(hidden, kv_down)
+    (model.py:70), which attention.py:181-185 stores as cat(k_codes, v_codes) at the
+    token's slot. float64 [n, W + rv]."""
+    return hidden.astype(np.float64) @ kv_down.astype(np.float64).T
