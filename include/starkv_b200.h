@@ -32,7 +32,9 @@
 extern "C" {
 #endif
 
-#define STARKV_ABI_VERSION 2
+/* 3: adds starkv_prefill_attention and starkv_kv_down_cache_write (2: starkv_fold_q
+ * takes a status word) */
+#define STARKV_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define STARKV_API __attribute__((visibility("default")))

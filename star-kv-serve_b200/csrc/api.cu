@@ -567,7 +567,7 @@ size_t starkv_abi_sizeof(int32_t which) {
   }
 }
 
-const char* starkv_version(void) { return "starkv_b200 1.1 (abi 2, sm_100a)"; }
+const char* starkv_version(void) { return "starkv_b200 1.2 (abi 3, sm_100a)"; }
 
 const char* starkv_strerror(int status) {
   switch (status) {
