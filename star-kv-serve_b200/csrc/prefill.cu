@@ -5,16 +5,17 @@
 // One CTA per (128-query tile of a prompt, query head). Per 128-key tile j of the
 // causal range:
 //   S_j = Q . K_j^T       tcgen05 (M = 128 queries, N = 128 keys, K = 128 dims),
-//                         f32 in TMEM, double-buffered so S_{j+1} is computed while
-//                         the softmax reads S_j;
+//                         f32 in TMEM, three buffers: S_{j+2} is issued right after
+//                         the P.V of tile j, so it runs while the softmax works on
+//                         S_{j+1} and never delays a P.V;
 //   P_j = exp(S_j - m)    online softmax by 4 warps (one query row per thread, a
 //                         TMEM lane each), the running output rescaled in TMEM when
 //                         a row's max grows by more than 2^8; P_j (bf16 / f16)
 //                         written to shared memory in the 128-byte-swizzled K-major
 //                         MMA layout;
 //   O  += P_j . V_j       tcgen05 (N = 128 dims, K = 128 keys), f32 in TMEM.
-// Q, K and V tiles come by TMA (128-byte swizzle, two 64-dim boxes per tile); K / V
-// are double-buffered. The last tile is masked causally (key > query) and every
+// Q, K and V tiles come by TMA (128-byte swizzle, two 64-dim boxes per tile); K and
+// V have two slots each, freed by the S and the P.V that read them. The last tile is masked causally (key > query) and every
 // tile by the prompt length.
 //
 // Warps: 0 TMA producer, 1 TMEM owner and MMA issuer, 2-5 softmax (TMEM lane
@@ -33,18 +34,21 @@ constexpr int kThreads = 192;
 
 struct PrefillCtl {
   uint64_t q_full;
-  uint64_t kv_full[2], kv_empty[2];
-  uint64_t s_full[2], s_free[2];
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[3], s_free[3];
   uint64_t p_full, o_done, drain;
   uint32_t tmem_base;
   int abort_flag;
   int prompt, tile, start, len;
 };
 
-// Shared memory: Q | K0 V0 | K1 V1 | P, each 32 KB and 1024-aligned, then control.
+// Shared memory: Q | K0 K1 | V0 V1 | P, each 32 KB and 1024-aligned, then control.
+// TMEM: three S buffers (columns 0, 128, 256) and the output (384).
 constexpr int kSmemQ = 0;
-constexpr int kSmemKV = kTileBytes;
-constexpr int kSmemP = kSmemKV + 4 * kTileBytes;
+constexpr int kSmemK = kTileBytes;
+constexpr int kSmemV = kSmemK + 2 * kTileBytes;
+constexpr int kSmemP = kSmemV + 2 * kTileBytes;
+constexpr int kOCol = 3 * kRows;
 constexpr int kSmemCtl = kSmemP + kTileBytes;
 constexpr int kSmemBytes = kSmemCtl + (int)sizeof(PrefillCtl) + 1024;
 
@@ -131,8 +135,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     ctl->prompt = prompt; ctl->tile = tile; ctl->start = start; ctl->len = len;
     mbar_init(&ctl->q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&ctl->kv_full[s], 1);
-      mbar_init(&ctl->kv_empty[s], 1);
+      mbar_init(&ctl->k_full[s], 1);
+      mbar_init(&ctl->k_empty[s], 1);
+      mbar_init(&ctl->v_full[s], 1);
+      mbar_init(&ctl->v_empty[s], 1);
+    }
+    for (int s = 0; s < 3; ++s) {
       mbar_init(&ctl->s_full[s], 1);
       mbar_init(&ctl->s_free[s], 4);
     }
@@ -162,23 +170,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&ctl->q_full, kTileBytes);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(smem + kSmemQ + h * kHalfBytes, &tm_q, &ctl->q_full, 64 * h, hq, start + kRows * qt);
-        int last[2] = {-1, -1};   // last load issued into each stage
+        // K and V tiles in separate rings: K_j's slot frees when S_j is done, V_j's when
+        // the P.V of tile j is, so the next S is never queued behind a P.V
+        int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};   // last load issued into each slot
         for (int j = 0; j < nt; ++j) {
           const int s = j & 1;
-          if (!mbar_wait(&ctl->kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-          last[s] = j;
-          uint8_t* kd = smem + kSmemKV + s * 2 * kTileBytes;
-          uint8_t* vd = kd + kTileBytes;
-          mbar_arrive_expect_tx(&ctl->kv_full[s], 2 * kTileBytes);
-          for (int h = 0; h < 2; ++h) {
-            tma_load_3d(kd + h * kHalfBytes, &tm_k, &ctl->kv_full[s], 64 * h, hk, start + kRows * j);
-            tma_load_3d(vd + h * kHalfBytes, &tm_v, &ctl->kv_full[s], 64 * h, hv, start + kRows * j);
-          }
+          if (!mbar_wait(&ctl->k_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+          last_k[s] = j;
+          uint8_t* kd = smem + kSmemK + s * kTileBytes;
+          mbar_arrive_expect_tx(&ctl->k_full[s], kTileBytes);
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(kd + h * kHalfBytes, &tm_k, &ctl->k_full[s], 64 * h, hk, start + kRows * j);
+          if (!mbar_wait(&ctl->v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+          last_v[s] = j;
+          uint8_t* vd = smem + kSmemV + s * kTileBytes;
+          mbar_arrive_expect_tx(&ctl->v_full[s], kTileBytes);
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(vd + h * kHalfBytes, &tm_v, &ctl->v_full[s], 64 * h, hv, start + kRows * j);
         }
         // every copy has landed before the CTA may exit (consumed ones return at once)
         drain_wait(&ctl->q_full, 0, p.status);
-        for (int s = 0; s < 2; ++s)
-          if (last[s] >= 0) drain_wait(&ctl->kv_full[s], (last[s] >> 1) & 1, p.status);
+        for (int s = 0; s < 2; ++s) {
+          if (last_k[s] >= 0) drain_wait(&ctl->k_full[s], (last_k[s] >> 1) & 1, p.status);
+          if (last_v[s] >= 0) drain_wait(&ctl->v_full[s], (last_v[s] >> 1) & 1, p.status);
+        }
       }
     } else if (warp == 1) {
       // ================= MMA issuer =================
@@ -187,37 +202,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t idesc_s = instr_desc_f16(fmt, 0, 0, kRows, kRows);        // Q . K^T, both K-major
         const uint32_t idesc_o = instr_desc_f16(fmt, 0, 1, kRows, 128);          // P . V, V MN-major
         const uint32_t q_addr = smem_u32(smem + kSmemQ), p_addr = smem_u32(smem + kSmemP);
+        // S_j into TMEM buffer j % 3; S_0 and S_1 first, then after each P.V_j the
+        // S two tiles ahead, so a P.V never waits behind an S in the tensor pipe
+        auto issue_s = [&](int j) -> bool {
+          const int s = j & 1, b = j % 3;
+          if (!mbar_wait(&ctl->k_full[s], (j >> 1) & 1, abort_flag, p.status) ||
+              !mbar_wait(&ctl->s_free[b], ((j / 3) & 1) ^ 1, abort_flag, p.status))
+            return false;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(smem + kSmemK + s * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tmem + b * kRows, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s, kk > 0);
+          umma_commit(&ctl->s_full[b]);
+          umma_commit(&ctl->k_empty[s]);
+          return true;
+        };
         bool ok = mbar_wait(&ctl->q_full, 0, abort_flag, p.status);
-        for (int j = 0; ok && j <= nt; ++j) {
-          if (j < nt) {
-            const int s = j & 1;
-            if (!mbar_wait(&ctl->kv_full[s], (j >> 1) & 1, abort_flag, p.status) ||
-                !mbar_wait(&ctl->s_free[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t k_addr = smem_u32(smem + kSmemKV + s * 2 * kTileBytes);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_f16(tmem + s * kRows, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s, kk > 0);
-            umma_commit(&ctl->s_full[s]);
+        for (int j = 0; ok && j < 2 && j < nt; ++j) ok = issue_s(j);
+        for (int j = 0; ok && j < nt; ++j) {
+          const int s = j & 1;
+          if (!mbar_wait(&ctl->p_full, j & 1, abort_flag, p.status) ||
+              !mbar_wait(&ctl->v_full[s], (j >> 1) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
           }
-          if (j >= 1) {
-            const int jp = j - 1, s = jp & 1;
-            if (!mbar_wait(&ctl->p_full, jp & 1, abort_flag, p.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t v_addr = smem_u32(smem + kSmemKV + s * 2 * kTileBytes + kTileBytes);
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + kSmemV + s * kTileBytes);
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_f16(tmem + 2 * kRows, kmajor_desc(p_addr, kk),
-                       smem_desc(v_addr + kk * 2048, kHalfBytes, 1024, kSwizzle128B), idesc_o, jp > 0 || kk > 0);
-            umma_commit(&ctl->o_done);
-            umma_commit(&ctl->kv_empty[s]);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tmem + kOCol, kmajor_desc(p_addr, kk),
+                     smem_desc(v_addr + kk * 2048, kHalfBytes, 1024, kSwizzle128B), idesc_o, j > 0 || kk > 0);
+          umma_commit(&ctl->o_done);
+          umma_commit(&ctl->v_empty[s]);
+          if (j + 2 < nt) ok = issue_s(j + 2);
         }
         // every MMA issued here has completed before TMEM is freed
         umma_commit(&ctl->drain);
@@ -233,8 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < nt; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&ctl->s_full[s], (j >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        const int s = j % 3;   // S buffer of tile j
+        if (!mbar_wait(&ctl->s_full[s], (j / 3) & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         uint32_t sr[4][32];
 #pragma unroll
@@ -312,11 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
-            tmem_ld32_issue(lane_base + 2 * kRows + 32 * c, o);
+            tmem_ld32_issue(lane_base + kOCol + 32 * c, o);
             tmem_wait(o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(lane_base + 2 * kRows + 32 * c, o);
+            tmem_st32(lane_base + kOCol + 32 * c, o);
           }
           tmem_st_wait();
         }
@@ -332,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32_issue(lane_base + 2 * kRows + 32 * c, o);
+          tmem_ld32_issue(lane_base + kOCol + 32 * c, o);
           tmem_wait(o);
           if (qi < L) {
 #pragma unroll
